@@ -1,0 +1,93 @@
+"""Generate golden fixtures from the UNCHANGED reference CPU executable.
+
+Run in the build container (needs ``/root/reference`` and ``make -C oracle ref``):
+
+    python tests/golden/make_golden.py
+
+For each case it writes a seeded float32 WAV, runs ``oracle/_ref/vocalarc-separation``
+(built from native/vocalarc_separation.c by oracle/Makefile) over the JSONL
+``load``/``separate`` protocol with ``VOCALARC_DEBUG_DUMP`` set
+(vocalarc_separation.c:67-74, dumps at :1348, :1352, :1427, :1441), and stores
+the stage tensors and the vocals WAV in ``tests/golden/<case>.npz``.  The model
+pack is the seeded synthetic pack ``modelpack.TEST_RECIPE``; its sha256 is
+stored so a test can confirm that regeneration is bit-identical.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from karaoke_platform_sidecar_native_b200 import fixtures, modelpack  # noqa: E402
+
+EXE = os.path.join(ROOT, "oracle", "_ref", "vocalarc-separation")
+
+#: case name -> (samples, seed, frames kept from the feature dumps)
+CASES = {
+    "clip_a": (13230, 0, (0, 1, 13, 25)),     # 0.3 s, T = 26
+    "clip_t1": (300, 3, (0,)),                 # T = 1, length < NFFT/2 (multi-reflect)
+    "clip_t2": (1000, 4, (0, 1)),              # T = 2
+}
+BANDS_KEPT = (0, 24, 60, 88, 89)
+
+
+def run_reference(pack: str, wav: str, vocals: str, dump: str, threads: int = 8) -> dict:
+    requests = [
+        {"id": 1, "type": "load"},
+        {"id": 2, "type": "separate", "inputPath": wav, "vocalsPath": vocals},
+        {"id": 3, "type": "shutdown"},
+    ]
+    env = dict(os.environ, VOCALARC_DEBUG_DUMP=dump)
+    proc = subprocess.run([EXE, "--model", pack, "--threads", str(threads)],
+                          input="".join(json.dumps(r) + "\n" for r in requests),
+                          capture_output=True, text=True, env=env, check=True)
+    lines = [json.loads(x) for x in proc.stdout.splitlines() if x.strip()]
+    assert lines[1]["ok"], proc.stdout
+    return lines[1]
+
+
+def main() -> None:
+    pack = modelpack.pack_path(modelpack.TEST_RECIPE)
+    digest = hashlib.sha256(open(pack, "rb").read()).hexdigest()
+    for name, (samples, seed, frames_kept) in CASES.items():
+        with tempfile.TemporaryDirectory() as tmp:
+            audio = fixtures.tone_mix(samples / fixtures.RATE, seed)
+            assert audio.shape[1] == samples
+            wav = os.path.join(tmp, "in.wav")
+            fixtures.write_wav_f32(wav, audio)
+            vocals_path = os.path.join(tmp, "vocals.wav")
+            prefix = os.path.join(tmp, "d")
+            reply = run_reference(pack, wav, vocals_path, prefix)
+            frames = reply["frames"]
+
+            def dump(stage, shape):
+                return np.fromfile(f"{prefix}-{stage}.f32", dtype=np.float32).reshape(shape)
+
+            source = dump("source", (1025, 2, frames, 2))
+            band = dump("band", (90, frames, 256))
+            f1 = dump("features1", (frames, 90, 256))
+            f16 = dump("features16", (frames, 90, 256))
+            mask = dump("mask", (1025, 2, frames, 2))
+            vocals = fixtures.read_wav_f32(vocals_path)
+            np.savez_compressed(
+                os.path.join(HERE, f"{name}.npz"),
+                audio=audio, source=source, mask=mask, vocals=vocals,
+                band=band[list(BANDS_KEPT)], bands_kept=np.array(BANDS_KEPT),
+                features1=f1[list(frames_kept)], features16=f16[list(frames_kept)],
+                frames_kept=np.array(frames_kept), frames=np.array(frames),
+                pack_sha256=np.array(digest), seed=np.array(seed))
+            print(name, "frames", frames, "vocals rms", float(np.sqrt((vocals ** 2).mean())))
+
+
+if __name__ == "__main__":
+    main()
