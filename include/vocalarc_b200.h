@@ -1,0 +1,87 @@
+/* Additive extension of the provider interface (no counterpart in the
+ * reference's native_gpu.h).
+ *
+ * The reference ABI stops at the transformer stack and the mask: the host
+ * still runs the STFT (vocalarc_separation.c:1066), the band split (:917) and
+ * the iSTFT (:1132) serially on the CPU.  These entry points run the complete
+ * forward_model (vocalarc_separation.c:1342-1445) on the device -- STFT, band
+ * split, 16 x 2 axial blocks, mask head, iSTFT -- and the chunked overlap-add
+ * of the ONNX sidecar (Separator::demix, onnx/native/onnx_sidecar.cpp:725-782).
+ *
+ * All functions return 1 on success and 0 on failure (message on stderr),
+ * like the reference provider.  Audio is planar float32 [2][length] at 44.1 kHz.
+ */
+#ifndef VOCALARC_B200_H
+#define VOCALARC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "native_gpu.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Provider bound to CUDA device `device` (native_gpu_create binds device 0,
+   or VOCALARC_GPU_DEVICE when set). NULL when the device is not sm_100. */
+native_gpu *vocalarc_b200_create(int device);
+
+/* Parse a VSCNAT01 pack (layout of model_parse, vocalarc_separation.c:528-589)
+   and keep every weight resident on the device in its kernel layout. The blob
+   is not retained. */
+int vocalarc_b200_load_model(native_gpu *gpu, const void *pack, size_t bytes);
+
+/* Whole-clip forward: frames = length/512 + 1, exactly forward_model. */
+int vocalarc_b200_separate(native_gpu *gpu, const float *audio, int length, float *vocals);
+
+/* Chunked forward: reflect border, chunks of chunk_samples (<= 0 selects
+   881559) at step chunk/2, native forward per chunk, linear fade over the last
+   chunk/10 samples, weights of the first and final predict batch forced to 1
+   (model_batch = the ONNX model's batch size, 1 or 2), divide, crop. */
+int vocalarc_b200_separate_chunked(native_gpu *gpu, const float *audio, int length,
+                                   int chunk_samples, int model_batch, float *vocals);
+
+/* Device-pointer variants on the provider's stream; they return after
+   enqueueing (call vocalarc_b200_synchronize).  `tracks` planar clips of
+   `length` samples each are laid out back to back ([tracks][2][length]). */
+int vocalarc_b200_separate_device(native_gpu *gpu, const float *d_audio, int tracks, int length,
+                                  int chunked, int chunk_samples, int model_batch, float *d_vocals);
+int vocalarc_b200_synchronize(native_gpu *gpu);
+/* The provider's cudaStream_t, for callers that order their own work after it. */
+void *vocalarc_b200_stream(native_gpu *gpu);
+/* First device-side error code recorded by a kernel (0 = none) and clears it. */
+int vocalarc_b200_take_device_error(native_gpu *gpu);
+/* 0 = fp16 operands (default), 1 = bf16 operands; both accumulate in fp32. */
+int vocalarc_b200_set_precision(native_gpu *gpu, int bf16);
+
+/* ---- stage entry points (device pointers, provider stream) used by the
+   parity tests to check each kernel against the CPU oracle ---- */
+
+/* C[M][N] = A[M][K] * B[N][K]^T (16-bit A, B), epilogue 0 = 16-bit store
+   (+bias), 1 = bias+GELU, 6 = fp32 store.  M >= 1, N % 256 == 0, K % 64 == 0. */
+int vocalarc_b200_stage_gemm(native_gpu *gpu, int epilogue, const void *a, const void *b, int m, int n,
+                             int k, const float *bias, void *out);
+/* Gated attention over qkv [rows][1536] (16-bit, RoPE already applied),
+   gates [rows][8]; rows = d3*d2*d1 tokens; positions along dim `pos_dim`
+   (1 or 2) of the (d1, d2, d3) token grid. Writes out [rows][512]. */
+int vocalarc_b200_stage_attention(native_gpu *gpu, const void *qkv, const float *gates, void *out,
+                                  int d1, int d2, int d3, int pos_dim);
+/* STFT of `segments` whole clips [segments][2][length] -> spec [segments][T][1025][2][2]. */
+int vocalarc_b200_stage_stft(native_gpu *gpu, const float *audio, int segments, int length, float *spec);
+/* iSTFT of spec*mask (both [segments][T][1025][2][2]) -> [segments][2][length]. */
+int vocalarc_b200_stage_istft(native_gpu *gpu, const float *spec, const float *mask, int segments,
+                              int length, float *audio);
+/* Band split of spec (loaded model) -> x [segments][90][T][256] fp32. */
+int vocalarc_b200_stage_band_split(native_gpu *gpu, const float *spec, int segments, int frames, float *x);
+/* One transformer block (loaded model, layer, axis 0 = time / 1 = band) in
+   place on x [segments][90][T][256]. */
+int vocalarc_b200_stage_block(native_gpu *gpu, float *x, int segments, int frames, int layer, int axis);
+/* Final norm + mask head (loaded model): x -> mask [segments][T][1025][2][2]. */
+int vocalarc_b200_stage_mask(native_gpu *gpu, const float *x, int segments, int frames, float *mask);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,1163 @@
+// Host runtime of the sm_100a provider: device context, weight conversion,
+// workspace, forward orchestration and the C ABI (native_gpu.h plus the
+// additive vocalarc_b200.h extension).
+//
+// Layout in HBM: the residual stream is one fp32 token matrix in band-major
+// order, rows (segment * 90 + band) * T + frame, 256 columns.  Both axial
+// blocks run on that same buffer: GEMMs are row-wise, and the attention
+// kernel addresses a sequence (a band over time, or a frame over bands)
+// through a 4-D TMA tensor map, so the reference's transpose kernels
+// (native_gpu_cuda.cu:428-451) disappear.  16-bit copies feed the tensor
+// cores (normed rows, q/k/v, gated attention, FFN hidden); the mask head reads
+// the band-major rows directly as its per-band A operand.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "vab_internal.h"
+#include "vocalarc_b200.h"
+
+using namespace vab;
+
+namespace {
+
+const int kBandFreqs[kBands] = {
+    2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,
+    4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,
+    4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  12, 12, 12, 12, 12, 12, 12, 12, 12, 12, 12, 12,
+    12, 12, 12, 12, 24, 24, 24, 24, 24, 24, 24, 24, 48, 48, 48, 48, 128, 129};
+
+int band_first(int band) {
+  int f = 0;
+  for (int b = 0; b < band; ++b) f += kBandFreqs[b];
+  return f;
+}
+int round16(int x) { return (x + 15) & ~15; }
+
+bool env_is_off(const char* name) {
+  const char* v = getenv(name);
+  return v != nullptr && (strcmp(v, "0") == 0 || strcmp(v, "false") == 0 || strcmp(v, "off") == 0);
+}
+
+// ------------------------------------------------------------------ weights
+// Unpacks the reference's 32-lane packed layout (vocalarc_separation.c:428-457)
+// into W[out][in].
+void unpack_packed(const float* packed, int in, int out, std::vector<float>& w) {
+  w.assign(static_cast<size_t>(in) * out, 0.f);
+  const int full = (out / 32) * 32;
+  for (int tile = 0; tile < full; tile += 32) {
+    const float* src = packed + static_cast<size_t>(tile / 32) * in * 32;
+    for (int i = 0; i < in; ++i)
+      for (int lane = 0; lane < 32; ++lane) w[static_cast<size_t>(tile + lane) * in + i] = src[static_cast<size_t>(i) * 32 + lane];
+  }
+  if (full < out) {
+    const int tail = out - full;
+    const float* src = packed + static_cast<size_t>(out / 32) * in * 32;
+    for (int i = 0; i < in; ++i)
+      for (int lane = 0; lane < tail; ++lane) w[static_cast<size_t>(full + lane) * in + i] = src[static_cast<size_t>(i) * tail + lane];
+  }
+}
+
+void to16(const std::vector<float>& w, bool bf16, std::vector<uint16_t>& out) {
+  out.resize(w.size());
+  for (size_t i = 0; i < w.size(); ++i) {
+    if (bf16) {
+      __nv_bfloat16 h = __float2bfloat16_rn(w[i]);
+      memcpy(&out[i], &h, 2);
+    } else {
+      __half h = __float2half_rn(w[i]);
+      memcpy(&out[i], &h, 2);
+    }
+  }
+}
+
+uint64_t fingerprint(const float* p, size_t n) {
+  uint64_t h = 1469598103934665603ull ^ reinterpret_cast<uintptr_t>(p) ^ (n * 1099511628211ull);
+  const size_t picks[8] = {0, 1, 2, 3, n / 2, n - 3, n - 2, n - 1};
+  for (size_t i = 0; i < 8; ++i) {
+    uint32_t bits;
+    memcpy(&bits, p + (picks[i] < n ? picks[i] : 0), 4);
+    h = (h ^ bits) * 1099511628211ull;
+  }
+  return h;
+}
+
+struct DeviceBuffer {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+struct BlockW {
+  void* qkv = nullptr;
+  void* out = nullptr;
+  void* ff1 = nullptr;
+  void* ff2 = nullptr;
+  float* gamma = nullptr;
+  float* ff_gamma = nullptr;
+  float* gate_w = nullptr;
+  float* gate_b = nullptr;
+  float* ff1_b = nullptr;
+  float* ff2_b = nullptr;
+  CUtensorMap m_qkv, m_out, m_ff1, m_ff2;
+};
+
+struct CachedBlock {
+  native_gpu_transformer_weights key;
+  uint64_t print = 0;
+  int bf16 = 0;
+  void* mem = nullptr;
+  BlockW w;
+};
+
+struct MaskW {
+  void* w1 = nullptr;
+  float* b1 = nullptr;
+  void* w2 = nullptr;
+  float* b2 = nullptr;
+  float* final_gamma = nullptr;
+  int w2_off[kBands];
+  int w2_rows[kBands];
+  int w2_total = 0;
+  CUtensorMap m_w1, m_w2;
+};
+
+struct BandW {
+  float* wt = nullptr;          // per band [d_b][256]
+  long long* wt_off = nullptr;  // [90]
+  float* gamma = nullptr;       // [4100]
+  int* gamma_off = nullptr;     // [91]
+  float* bias = nullptr;        // [90][256]
+};
+
+// Bump allocator over one cudaMalloc.
+struct Arena {
+  char* base = nullptr;
+  size_t cap = 0, used = 0;
+  void* take(size_t bytes) {
+    const size_t off = (used + 1023) & ~size_t(1023);
+    if (off + bytes > cap) return nullptr;
+    used = off + bytes;
+    return base + off;
+  }
+};
+
+}  // namespace
+
+struct native_gpu {
+  int device = 0;
+  int enabled = 0;
+  int bf16 = 0;
+  int sm_count = 148;
+  int debug = 0;
+  char device_name[256] = {0};
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;
+  float* d_window = nullptr;
+  float2* d_twiddle = nullptr;
+  float2* d_rope = nullptr;
+  int rope_len = 0;
+  // workspace (grow-only)
+  long long ws_tokens = 0;
+  float* x = nullptr;
+  float* x_alt = nullptr;
+  void* normed = nullptr;
+  void* qkv = nullptr;
+  void* attn = nullptr;
+  float* gates = nullptr;
+  long long ws_frames = 0;  // segments * frames
+  float* spec = nullptr;
+  float* mask = nullptr;
+  float* frames_buf = nullptr;
+  long long ws_seg = 0;     // segments * 2 * segment samples
+  float* seg_out = nullptr;
+  long long ws_audio = 0;
+  float* audio_in = nullptr;
+  float* audio_out = nullptr;
+  // mask tile tables
+  int tiles_frames = 0;
+  int4* d_tiles1 = nullptr;
+  int n_tiles1 = 0;
+  int4* d_tiles2 = nullptr;
+  int n_tiles2 = 0;
+  // loaded model (vocalarc_b200_load_model)
+  int model_loaded = 0;
+  void* model_mem = nullptr;
+  BlockW blocks[kDepth][2];
+  BandW band;
+  MaskW maskw;
+  // ABI caches
+  std::vector<CachedBlock> block_cache;
+  void* abi_mask_mem = nullptr;
+  uint64_t abi_mask_print = 0;
+  int abi_mask_bf16 = -1;
+  MaskW abi_mask;
+  // resident session of the reference ABI
+  int resident_active = 0;
+  long long resident_tokens = 0;
+  int phys_s = 0, phys_l = 0;   // layout of the device buffer: [phys_s][phys_l]
+  int transposed = 0;           // logical layout = [phys_l][phys_s] when set
+};
+
+namespace {
+
+bool cuda_ok(native_gpu* g, cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return true;
+  fprintf(stderr, "vocalarc-b200: %s failed: %s; falling back to CPU\n", what, cudaGetErrorString(e));
+  g->enabled = 0;
+  return false;
+}
+
+bool launched(native_gpu* g, cudaError_t e, const char* what) {
+  if (!cuda_ok(g, e, what)) return false;
+  if (g->debug) {
+    if (!cuda_ok(g, cudaStreamSynchronize(g->stream), what)) return false;
+    int err = 0;
+    cudaMemcpy(&err, g->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    fprintf(stderr, "vocalarc-b200: %s ok (device error %d)\n", what, err);
+  }
+  return true;
+}
+
+// Synchronises and turns a recorded device-side wait timeout into a failure.
+bool sync_and_check(native_gpu* g, const char* what) {
+  if (!cuda_ok(g, cudaStreamSynchronize(g->stream), what)) return false;
+  int err = 0;
+  if (!cuda_ok(g, cudaMemcpy(&err, g->d_err, sizeof(int), cudaMemcpyDeviceToHost), what)) return false;
+  if (err != 0) {
+    fprintf(stderr, "vocalarc-b200: %s: kernel gave up waiting (code %d); falling back to CPU\n", what, err);
+    cudaMemset(g->d_err, 0, sizeof(int));
+    g->enabled = 0;
+    return false;
+  }
+  return true;
+}
+
+template <typename P>
+bool grow(native_gpu* g, P** ptr, size_t bytes, const char* what) {
+  if (*ptr != nullptr) cudaFree(*ptr);
+  *ptr = nullptr;
+  return cuda_ok(g, cudaMalloc(reinterpret_cast<void**>(ptr), bytes), what);
+}
+
+bool ensure_tokens(native_gpu* g, long long tokens) {
+  if (tokens <= g->ws_tokens) return true;
+  g->ws_tokens = 0;
+  const size_t t = static_cast<size_t>(tokens);
+  if (!grow(g, &g->x, t * kDim * 4, "cudaMalloc(x)") || !grow(g, &g->x_alt, t * kDim * 4, "cudaMalloc(x_alt)") ||
+      !grow(g, &g->normed, t * kDim * 2, "cudaMalloc(normed)") ||
+      !grow(g, &g->qkv, t * kQkvDim * 2, "cudaMalloc(qkv)") ||
+      !grow(g, &g->attn, t * kDimInner * 2, "cudaMalloc(attn)") ||
+      !grow(g, &g->gates, t * kHeads * 4, "cudaMalloc(gates)"))
+    return false;
+  g->ws_tokens = tokens;
+  return true;
+}
+
+bool ensure_frames(native_gpu* g, long long seg_frames) {
+  if (seg_frames <= g->ws_frames) return true;
+  g->ws_frames = 0;
+  const size_t f = static_cast<size_t>(seg_frames);
+  if (!grow(g, &g->spec, f * kFreqBins * 4 * 4, "cudaMalloc(spec)") ||
+      !grow(g, &g->mask, f * kFreqBins * 4 * 4, "cudaMalloc(mask)") ||
+      !grow(g, &g->frames_buf, f * 2 * kNfft * 4, "cudaMalloc(frames)"))
+    return false;
+  g->ws_frames = seg_frames;
+  return true;
+}
+
+bool ensure_seg(native_gpu* g, long long samples) {
+  if (samples <= g->ws_seg) return true;
+  g->ws_seg = 0;
+  if (!grow(g, &g->seg_out, static_cast<size_t>(samples) * 4, "cudaMalloc(seg_out)")) return false;
+  g->ws_seg = samples;
+  return true;
+}
+
+bool ensure_audio(native_gpu* g, long long samples) {
+  if (samples <= g->ws_audio) return true;
+  g->ws_audio = 0;
+  if (!grow(g, &g->audio_in, static_cast<size_t>(samples) * 4, "cudaMalloc(audio_in)") ||
+      !grow(g, &g->audio_out, static_cast<size_t>(samples) * 4, "cudaMalloc(audio_out)"))
+    return false;
+  g->ws_audio = samples;
+  return true;
+}
+
+// cos/sin table exactly as apply_rotary builds it (vocalarc_separation.c:726-731,
+// frequencies from fill_frequencies :1312-1314), float arithmetic and libm.
+bool ensure_rope(native_gpu* g, int positions) {
+  if (positions <= g->rope_len) return true;
+  const int n = positions < 128 ? 128 : positions;
+  std::vector<float2> table(static_cast<size_t>(n) * 32);
+  float freq[32];
+  for (int i = 0; i < 32; ++i) freq[i] = 1.0f / powf(10000.0f, static_cast<float>(2 * i) / kDimHead);
+  for (int p = 0; p < n; ++p)
+    for (int i = 0; i < 32; ++i) {
+      const float angle = static_cast<float>(p) * freq[i];
+      table[static_cast<size_t>(p) * 32 + i] = make_float2(cosf(angle), sinf(angle));
+    }
+  g->rope_len = 0;
+  if (!grow(g, &g->d_rope, table.size() * sizeof(float2), "cudaMalloc(rope)")) return false;
+  if (!cuda_ok(g, cudaMemcpy(g->d_rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope"))
+    return false;
+  g->rope_len = n;
+  return true;
+}
+
+bool make_map_rows(native_gpu* g, CUtensorMap* map, const void* base, long long rows, int k, int box_rows) {
+  (void)g;
+  return make_tmap_2d(map, base, 2, static_cast<uint64_t>(k), static_cast<uint64_t>(rows),
+                      static_cast<uint64_t>(k) * 2, 64, static_cast<uint32_t>(box_rows), true, g->bf16 != 0);
+}
+
+bool upload16(native_gpu* g, Arena& arena, const float* packed, int in, int out, void** dst, CUtensorMap* map,
+              int box_rows) {
+  std::vector<float> w;
+  std::vector<uint16_t> h;
+  unpack_packed(packed, in, out, w);
+  to16(w, g->bf16 != 0, h);
+  *dst = arena.take(h.size() * 2);
+  if (*dst == nullptr) return false;
+  if (!cuda_ok(g, cudaMemcpy(*dst, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "upload weight")) return false;
+  return make_map_rows(g, map, *dst, out, in, box_rows);
+}
+
+bool upload_f32(native_gpu* g, Arena& arena, const float* src, size_t count, float** dst) {
+  *dst = static_cast<float*>(arena.take(count * 4));
+  if (*dst == nullptr) return false;
+  return cuda_ok(g, cudaMemcpy(*dst, src, count * 4, cudaMemcpyHostToDevice), "upload vector");
+}
+
+constexpr size_t kBlockBytes = (static_cast<size_t>(kQkvDim) * kDim + kDim * kDimInner + 2 * kFfDim * kDim) * 2 +
+                               (kHeads * kDim + 3 * kDim + kHeads + kFfDim) * 4 + 16 * 1024;
+
+bool upload_block(native_gpu* g, Arena& arena, const native_gpu_transformer_weights& w, BlockW& b) {
+  std::vector<float> gw;
+  if (!upload16(g, arena, w.qkv, kDim, kQkvDim, &b.qkv, &b.m_qkv, 256) ||
+      !upload16(g, arena, w.out_weight, kDimInner, kDim, &b.out, &b.m_out, 256) ||
+      !upload16(g, arena, w.ff1_weight, kDim, kFfDim, &b.ff1, &b.m_ff1, 256) ||
+      !upload16(g, arena, w.ff2_weight, kFfDim, kDim, &b.ff2, &b.m_ff2, 256))
+    return false;
+  unpack_packed(w.gate_weight, kDim, kHeads, gw);
+  return upload_f32(g, arena, gw.data(), gw.size(), &b.gate_w) && upload_f32(g, arena, w.gamma, kDim, &b.gamma) &&
+         upload_f32(g, arena, w.ff_gamma, kDim, &b.ff_gamma) && upload_f32(g, arena, w.gate_bias, kHeads, &b.gate_b) &&
+         upload_f32(g, arena, w.ff1_bias, kFfDim, &b.ff1_b) && upload_f32(g, arena, w.ff2_bias, kDim, &b.ff2_b);
+}
+
+int mask_w2_rows_total() {
+  int total = 0;
+  for (int b = 0; b < kBands; ++b) total += round16(2 * 4 * kBandFreqs[b]);
+  return total;
+}
+
+constexpr size_t mask_bytes_estimate() {
+  return static_cast<size_t>(kBands) * kFfDim * kDim * 2 + kBands * kFfDim * 4 + 8400ull * kFfDim * 2 + 8400 * 4 +
+         kDim * 4 + 256 * 1024;
+}
+
+// Mask head weights: first layers stacked [90*1024][256]; second layers with
+// rows interleaved (value i, gate i) so the GLU pairs are adjacent columns,
+// each band padded to a multiple of 16 rows.
+bool upload_mask(native_gpu* g, Arena& arena, const native_gpu_mask_band* bands, const float* final_gamma, MaskW& m) {
+  const bool bf = g->bf16 != 0;
+  std::vector<float> w, all1(static_cast<size_t>(kBands) * kFfDim * kDim), b1(static_cast<size_t>(kBands) * kFfDim);
+  for (int b = 0; b < kBands; ++b) {
+    unpack_packed(bands[b].first_weight, kDim, kFfDim, w);
+    memcpy(&all1[static_cast<size_t>(b) * kFfDim * kDim], w.data(), w.size() * 4);
+    memcpy(&b1[static_cast<size_t>(b) * kFfDim], bands[b].first_bias, kFfDim * 4);
+  }
+  std::vector<uint16_t> h;
+  to16(all1, bf, h);
+  m.w1 = arena.take(h.size() * 2);
+  if (m.w1 == nullptr || !cuda_ok(g, cudaMemcpy(m.w1, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "mask w1"))
+    return false;
+  if (!make_map_rows(g, &m.m_w1, m.w1, static_cast<long long>(kBands) * kFfDim, kDim, 256)) return false;
+  if (!upload_f32(g, arena, b1.data(), b1.size(), &m.b1)) return false;
+  m.w2_total = mask_w2_rows_total();
+  std::vector<float> all2(static_cast<size_t>(m.w2_total) * kFfDim, 0.f), b2(m.w2_total, 0.f);
+  int off = 0;
+  for (int b = 0; b < kBands; ++b) {
+    const int d = bands[b].input_dim;
+    unpack_packed(bands[b].second_weight, kFfDim, 2 * d, w);
+    for (int i = 0; i < d; ++i) {
+      memcpy(&all2[static_cast<size_t>(off + 2 * i) * kFfDim], &w[static_cast<size_t>(i) * kFfDim], kFfDim * 4);
+      memcpy(&all2[static_cast<size_t>(off + 2 * i + 1) * kFfDim], &w[static_cast<size_t>(d + i) * kFfDim], kFfDim * 4);
+      b2[off + 2 * i] = bands[b].second_bias[i];
+      b2[off + 2 * i + 1] = bands[b].second_bias[d + i];
+    }
+    m.w2_off[b] = off;
+    m.w2_rows[b] = round16(2 * d);
+    off += m.w2_rows[b];
+  }
+  to16(all2, bf, h);
+  m.w2 = arena.take(h.size() * 2);
+  if (m.w2 == nullptr || !cuda_ok(g, cudaMemcpy(m.w2, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "mask w2"))
+    return false;
+  if (!make_map_rows(g, &m.m_w2, m.w2, m.w2_total, kFfDim, 16)) return false;
+  if (!upload_f32(g, arena, b2.data(), b2.size(), &m.b2)) return false;
+  return upload_f32(g, arena, final_gamma, kDim, &m.final_gamma);
+}
+
+bool ensure_mask_tiles(native_gpu* g, int frames, const MaskW& m) {
+  if (g->tiles_frames == frames && g->d_tiles1 != nullptr) return true;
+  std::vector<int4> t1, t2;
+  for (int b = 0; b < kBands; ++b)
+    for (int m0 = 0; m0 < frames; m0 += 128) {
+      const int mv = frames - m0 < 128 ? frames - m0 : 128;
+      for (int n0 = 0; n0 < kFfDim; n0 += 256) t1.push_back(make_tile(b * frames + m0, b * kFfDim + n0, n0, mv, 256, b));
+      for (int n0 = 0; n0 < m.w2_rows[b]; n0 += 256) {
+        const int ns = m.w2_rows[b] - n0 < 256 ? m.w2_rows[b] - n0 : 256;
+        t2.push_back(make_tile(b * frames + m0, m.w2_off[b] + n0, n0, mv, ns, b));
+      }
+    }
+  g->tiles_frames = 0;
+  if (!grow(g, &g->d_tiles1, t1.size() * sizeof(int4), "cudaMalloc(tiles)") ||
+      !grow(g, &g->d_tiles2, t2.size() * sizeof(int4), "cudaMalloc(tiles)"))
+    return false;
+  if (!cuda_ok(g, cudaMemcpy(g->d_tiles1, t1.data(), t1.size() * sizeof(int4), cudaMemcpyHostToDevice), "tiles") ||
+      !cuda_ok(g, cudaMemcpy(g->d_tiles2, t2.data(), t2.size() * sizeof(int4), cudaMemcpyHostToDevice), "tiles"))
+    return false;
+  g->n_tiles1 = static_cast<int>(t1.size());
+  g->n_tiles2 = static_cast<int>(t2.size());
+  g->tiles_frames = frames;
+  return true;
+}
+
+GemmArgs uniform_args(native_gpu* g, long long rows, int n, int k) {
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.m_rows = static_cast<int>(rows);
+  a.n_tiles = n / 256;
+  a.k_blocks = k / 64;
+  a.num_tiles = static_cast<int>((rows + 127) / 128) * a.n_tiles;
+  a.err = g->d_err;
+  a.pos_div = 1;
+  a.pos_mod = 1;
+  return a;
+}
+
+// ------------------------------------------------------------------ one axial block
+// Token grid (d1, d2, d3): row = (i3 * d2 + i2) * d1 + i1.  Positions run along
+// dim `pos_dim`; the RoPE position of row r is (r / pos_div) % pos_mod.
+struct AxisPlan {
+  int pos_dim, d1, d2, d3, sequences, length, pos_div, pos_mod;
+};
+
+bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan& ax) {
+  const bool bf = g->bf16 != 0;
+  if (!ensure_rope(g, ax.length)) return false;
+  if (!launched(g, launch_norm(g->x, tokens, w.gamma, w.gate_w, w.gate_b, g->normed, g->gates, bf, 0, 0, g->stream),
+                "norm+gates"))
+    return false;
+  CUtensorMap a;
+  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
+  GemmArgs args = uniform_args(g, tokens, kQkvDim, kDim);
+  args.out = g->qkv;
+  args.ldo = kQkvDim;
+  args.rope = g->d_rope;
+  args.pos_div = ax.pos_div;
+  args.pos_mod = ax.pos_mod;
+  args.rope_cols = 2 * kDimInner;
+  if (!launched(g, launch_gemm(kEpiQkvRope, bf, a, w.m_qkv, args, g->sm_count, g->stream), "qkv gemm")) return false;
+
+  CUtensorMap q4;
+  const uint64_t dims[4] = {static_cast<uint64_t>(kQkvDim), static_cast<uint64_t>(ax.d1),
+                            static_cast<uint64_t>(ax.d2), static_cast<uint64_t>(ax.d3)};
+  const uint64_t row_bytes = kQkvDim * 2ull;
+  const uint64_t strides[3] = {row_bytes, row_bytes * ax.d1, row_bytes * ax.d1 * ax.d2};
+  const uint32_t box[4] = {64u, ax.pos_dim == 1 ? 128u : 1u, ax.pos_dim == 2 ? 128u : 1u, 1u};
+  if (!make_tmap_4d(&q4, g->qkv, 2, dims, strides, box, bf)) return false;
+  AttnArgs at;
+  at.length = ax.length;
+  at.sequences = ax.sequences;
+  at.q_tiles = (ax.length + 127) / 128;
+  at.pos_dim = ax.pos_dim;
+  at.d1 = ax.d1;
+  at.d2 = ax.d2;
+  at.gates = g->gates;
+  at.out = g->attn;
+  at.err = g->d_err;
+  if (!launched(g, launch_attention(bf, q4, at, g->stream), "attention")) return false;
+
+  if (!make_map_rows(g, &a, g->attn, tokens, kDimInner, 128)) return false;
+  args = uniform_args(g, tokens, kDim, kDimInner);
+  args.resid = g->x;
+  args.ldr = kDim;
+  if (!launched(g, launch_gemm(kEpiResidual, bf, a, w.m_out, args, g->sm_count, g->stream), "out gemm")) return false;
+
+  if (!launched(g, launch_norm(g->x, tokens, w.ff_gamma, nullptr, nullptr, g->normed, nullptr, bf, 0, 0, g->stream),
+                "ff norm"))
+    return false;
+  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
+  args = uniform_args(g, tokens, kFfDim, kDim);
+  args.out = g->qkv;
+  args.ldo = kFfDim;
+  args.bias = w.ff1_b;
+  if (!launched(g, launch_gemm(kEpiGelu, bf, a, w.m_ff1, args, g->sm_count, g->stream), "ff1 gemm")) return false;
+  if (!make_map_rows(g, &a, g->qkv, tokens, kFfDim, 128)) return false;
+  args = uniform_args(g, tokens, kDim, kFfDim);
+  args.resid = g->x;
+  args.ldr = kDim;
+  args.bias = w.ff2_b;
+  return launched(g, launch_gemm(kEpiResidual, bf, a, w.m_ff2, args, g->sm_count, g->stream), "ff2 gemm");
+}
+
+// Final RMSNorm + mask MLPs over `segments` x 90 x frames band-major tokens.
+// remap: physical [frames][90] rows are re-ordered band-major by the norm.
+bool run_mask(native_gpu* g, const MaskW& m, int segments, int frames, bool frame_major_rows, bool ref_layout,
+              float* mask_out) {
+  const bool bf = g->bf16 != 0;
+  const long long tokens = static_cast<long long>(segments) * kBands * frames;
+  if (!launched(g, launch_norm(g->x, tokens, m.final_gamma, nullptr, nullptr, g->normed, nullptr, bf,
+                               frame_major_rows ? frames : 0, frame_major_rows ? kBands : 0, g->stream),
+                "final norm"))
+    return false;
+  if (!ensure_mask_tiles(g, frames, m)) return false;
+  CUtensorMap a;
+  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
+  GemmArgs args;
+  memset(&args, 0, sizeof(args));
+  args.k_blocks = kDim / 64;
+  args.tiles = g->d_tiles1;
+  args.tiles_per_chunk = g->n_tiles1;
+  args.chunk_rows = kBands * frames;
+  args.num_tiles = g->n_tiles1 * segments;
+  args.out = g->qkv;
+  args.ldo = kFfDim;
+  args.bias = m.b1;
+  args.err = g->d_err;
+  args.pos_div = args.pos_mod = 1;
+  if (!launched(g, launch_gemm(kEpiTanhBand, bf, a, m.m_w1, args, g->sm_count, g->stream), "mask gemm 1")) return false;
+  if (!make_map_rows(g, &a, g->qkv, tokens, kFfDim, 128)) return false;
+  args.k_blocks = kFfDim / 64;
+  args.tiles = g->d_tiles2;
+  args.tiles_per_chunk = g->n_tiles2;
+  args.num_tiles = g->n_tiles2 * segments;
+  args.b_box16 = 1;
+  args.out = mask_out;
+  args.ldo = 0;
+  args.bias = m.b2;
+  args.frames = frames;
+  args.mask_ref_layout = ref_layout ? 1 : 0;
+  return launched(g, launch_gemm(kEpiGluMask, bf, a, m.m_w2, args, g->sm_count, g->stream), "mask gemm 2");
+}
+
+AxisPlan time_axis(int segments, int frames) {
+  return AxisPlan{1, frames, kBands, segments, segments * kBands, frames, 1, frames};
+}
+AxisPlan band_axis(int segments, int frames) {
+  return AxisPlan{2, frames, kBands, segments, segments * frames, kBands, frames, kBands};
+}
+
+// Full forward of `segments` equal-length segments (T frames each).
+bool forward_segments(native_gpu* g, const float* d_audio, const SegmentMap& map, int segments, int frames,
+                      float* d_seg_out) {
+  const long long tokens = static_cast<long long>(segments) * kBands * frames;
+  if (!ensure_tokens(g, tokens) || !ensure_frames(g, static_cast<long long>(segments) * frames)) return false;
+  if (!launched(g, launch_stft(d_audio, map, segments, frames, g->d_window, g->d_twiddle, g->spec, g->stream), "stft"))
+    return false;
+  if (!launched(g, launch_band_split(g->spec, segments, frames, g->band.wt, g->band.wt_off, g->band.gamma,
+                                     g->band.gamma_off, g->band.bias, g->x, g->stream),
+                "band split"))
+    return false;
+  for (int layer = 0; layer < kDepth; ++layer) {
+    if (!run_block(g, g->blocks[layer][0], tokens, time_axis(segments, frames))) return false;
+    if (!run_block(g, g->blocks[layer][1], tokens, band_axis(segments, frames))) return false;
+  }
+  if (!run_mask(g, g->maskw, segments, frames, false, false, g->mask)) return false;
+  if (!launched(g, launch_istft_frames(g->spec, g->mask, segments, frames, g->d_window, g->d_twiddle, g->frames_buf,
+                                       g->stream),
+                "istft"))
+    return false;
+  return launched(g, launch_overlap_add(g->frames_buf, segments, frames, map.seg_length, g->d_window, d_seg_out,
+                                        g->stream),
+                  "overlap-add");
+}
+
+// Largest number of chunk-sized segments that fit comfortably in free memory.
+int max_segments(native_gpu* g, int frames, int seg_length) {
+  size_t free_b = 0, total_b = 0;
+  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return 1;
+  const double per_token = kDim * 4.0 * 2 + kDim * 2 + kQkvDim * 2 + kDimInner * 2 + kHeads * 4;
+  const double per_seg = per_token * kBands * frames + frames * (kFreqBins * 32.0 + 2 * kNfft * 4.0) +
+                         2.0 * seg_length * 4;
+  // Count what is already allocated as available for reuse.
+  const double have = g->ws_tokens * per_token;
+  const double budget = (static_cast<double>(free_b) + have) * 0.7 - 512.0 * 1024 * 1024;
+  int n = static_cast<int>(budget / per_seg);
+  if (n < 1) n = 1;
+  if (n > 64) n = 64;
+  return n;
+}
+
+bool separate_device_impl(native_gpu* g, const float* d_audio, int tracks, int length, int chunked, int chunk_samples,
+                          int model_batch, float* d_vocals) {
+  if (!g->model_loaded) {
+    fprintf(stderr, "vocalarc-b200: no model loaded (vocalarc_b200_load_model)\n");
+    return false;
+  }
+  if (length <= 0 || tracks <= 0) return false;
+  if (!chunked) {
+    const int frames = length / kHop + 1;
+    const int per_pass = max_segments(g, frames, length);
+    for (int t0 = 0; t0 < tracks; t0 += per_pass) {
+      const int n = tracks - t0 < per_pass ? tracks - t0 : per_pass;
+      const SegmentMap map = whole_clip_map(length);
+      // Whole clips write their overlap-add output straight into the vocals buffer.
+      if (!forward_segments(g, d_audio + static_cast<long long>(t0) * 2 * length, map, n, frames,
+                            d_vocals + static_cast<long long>(t0) * 2 * length))
+        return false;
+    }
+    return true;
+  }
+  const int chunk = chunk_samples > 0 ? chunk_samples : 881559;
+  const int step = chunk / 2;
+  const int border = chunk - step;
+  const bool padded = length > 2 * border && border > 0;
+  const int plen = padded ? length + 2 * border : length;
+  const int chunks = (plen + step - 1) / step;
+  const int frames = chunk / kHop + 1;
+  if (model_batch < 1) model_batch = 1;
+  if (!ensure_seg(g, static_cast<long long>(chunks) * 2 * chunk)) return false;
+  const int per_pass = max_segments(g, frames, chunk);
+  for (int tr = 0; tr < tracks; ++tr) {
+    const float* audio = d_audio + static_cast<long long>(tr) * 2 * length;
+    for (int c0 = 0; c0 < chunks; c0 += per_pass) {
+      const int n = chunks - c0 < per_pass ? chunks - c0 : per_pass;
+      const SegmentMap mm = demix_map(length, chunk, padded ? border : 0, plen, step, c0);
+      if (!forward_segments(g, audio, mm, n, frames, g->seg_out + static_cast<long long>(c0) * 2 * chunk)) return false;
+    }
+    const SegmentMap dm = demix_map(length, chunk, padded ? border : 0, plen, step, 0);
+    if (!launched(g, launch_demix(g->seg_out, dm, chunks, model_batch,
+                                  d_vocals + static_cast<long long>(tr) * 2 * length, g->stream),
+                  "demix"))
+      return false;
+  }
+  return true;
+}
+
+struct PackCursor {
+  const unsigned char* p;
+  const unsigned char* end;
+  const float* next(uint64_t expected) {
+    if (static_cast<size_t>(end - p) < 8) return nullptr;
+    uint64_t count;
+    memcpy(&count, p, 8);
+    p += 8;
+    if (count != expected || static_cast<size_t>(end - p) < count * 4) return nullptr;
+    const float* r = reinterpret_cast<const float*>(p);
+    p += count * 4;
+    return r;
+  }
+};
+
+bool init_context(native_gpu* g, int device) {
+  g->device = device;
+  if (!cuda_ok(g, cudaSetDevice(device), "cudaSetDevice")) return false;
+  cudaDeviceProp prop;
+  if (!cuda_ok(g, cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties")) return false;
+  if (prop.major != 10 || prop.minor != 0) {
+    fprintf(stderr, "vocalarc-b200: device %d is sm_%d%d; these kernels need sm_100a\n", device, prop.major,
+            prop.minor);
+    return false;
+  }
+  snprintf(g->device_name, sizeof(g->device_name), "%s", prop.name);
+  g->sm_count = prop.multiProcessorCount;
+  g->debug = getenv("VOCALARC_GPU_DEBUG") != nullptr;
+  const char* prec = getenv("VOCALARC_B200_PRECISION");
+  g->bf16 = prec != nullptr && strcmp(prec, "bf16") == 0;
+  if (!cuda_ok(g, cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
+  if (!cuda_ok(g, cudaMalloc(reinterpret_cast<void**>(&g->d_err), sizeof(int)), "cudaMalloc(err)") ||
+      !cuda_ok(g, cudaMemset(g->d_err, 0, sizeof(int)), "cudaMemset(err)"))
+    return false;
+  // Periodic Hann window exactly as stft_channels computes it (vocalarc_separation.c:1052).
+  std::vector<float> window(kNfft);
+  for (int i = 0; i < kNfft; ++i)
+    window[i] = 0.5f - 0.5f * cosf(static_cast<float>(2.0 * 3.141592653589793238462643383279502884 * i / kNfft));
+  std::vector<float2> tw(1025);
+  for (int k = 0; k <= 1024; ++k) {
+    const double a = 2.0 * 3.141592653589793238462643383279502884 * k / 2048.0;
+    tw[k] = make_float2(static_cast<float>(cos(a)), static_cast<float>(-sin(a)));
+  }
+  if (!cuda_ok(g, cudaMalloc(reinterpret_cast<void**>(&g->d_window), kNfft * 4), "cudaMalloc(window)") ||
+      !cuda_ok(g, cudaMalloc(reinterpret_cast<void**>(&g->d_twiddle), 1025 * sizeof(float2)), "cudaMalloc(tw)") ||
+      !cuda_ok(g, cudaMemcpy(g->d_window, window.data(), kNfft * 4, cudaMemcpyHostToDevice), "window") ||
+      !cuda_ok(g, cudaMemcpy(g->d_twiddle, tw.data(), 1025 * sizeof(float2), cudaMemcpyHostToDevice), "twiddle"))
+    return false;
+  int first[kBands], dims[kBands];
+  for (int b = 0; b < kBands; ++b) {
+    first[b] = band_first(b);
+    dims[b] = 4 * kBandFreqs[b];
+  }
+  if (!cuda_ok(g, upload_band_tables(first, dims), "band tables")) return false;
+  g->enabled = 1;
+  return true;
+}
+
+void free_model(native_gpu* g) {
+  if (g->model_mem != nullptr) cudaFree(g->model_mem);
+  g->model_mem = nullptr;
+  g->model_loaded = 0;
+}
+
+native_gpu* create_on(int device) {
+  const char* mode = getenv("VOCALARC_GPU");
+  if (mode != nullptr && (strcmp(mode, "off") == 0 || strcmp(mode, "cpu") == 0)) return nullptr;
+  native_gpu* g = new native_gpu();
+  if (!init_context(g, device)) {
+    native_gpu_destroy(g);
+    return nullptr;
+  }
+  return g;
+}
+
+const BlockW* cached_block(native_gpu* g, const native_gpu_transformer_weights* w) {
+  const uint64_t print = fingerprint(w->qkv, static_cast<size_t>(kQkvDim) * kDim) ^
+                         (fingerprint(w->ff2_weight, static_cast<size_t>(kFfDim) * kDim) * 31);
+  for (auto& e : g->block_cache)
+    if (memcmp(&e.key, w, sizeof(*w)) == 0 && e.print == print && e.bf16 == g->bf16) return &e.w;
+  CachedBlock e;
+  e.key = *w;
+  e.print = print;
+  e.bf16 = g->bf16;
+  if (!cuda_ok(g, cudaMalloc(&e.mem, kBlockBytes), "cudaMalloc(block weights)")) return nullptr;
+  Arena arena{static_cast<char*>(e.mem), kBlockBytes, 0};
+  if (!upload_block(g, arena, *w, e.w)) {
+    cudaFree(e.mem);
+    return nullptr;
+  }
+  g->block_cache.push_back(e);
+  return &g->block_cache.back().w;
+}
+
+bool active(const native_gpu* g) { return g != nullptr && g->enabled; }
+
+}  // namespace
+
+// ==================================================================== C ABI
+extern "C" {
+
+native_gpu* native_gpu_create(void) {
+  int device = 0;
+  const char* d = getenv("VOCALARC_GPU_DEVICE");
+  if (d != nullptr && d[0] != '\0') device = atoi(d);
+  return create_on(device);
+}
+
+native_gpu* vocalarc_b200_create(int device) { return create_on(device); }
+
+void native_gpu_destroy(native_gpu* g) {
+  if (g == nullptr) return;
+  cudaSetDevice(g->device);
+  if (g->stream != nullptr) cudaStreamSynchronize(g->stream);
+  void* ptrs[] = {g->x, g->x_alt, g->normed, g->qkv, g->attn, g->gates, g->spec, g->mask, g->frames_buf,
+                  g->seg_out, g->audio_in, g->audio_out, g->d_tiles1, g->d_tiles2, g->d_err, g->d_window,
+                  g->d_twiddle, g->d_rope, g->abi_mask_mem};
+  for (void* p : ptrs)
+    if (p != nullptr) cudaFree(p);
+  for (auto& e : g->block_cache) cudaFree(e.mem);
+  free_model(g);
+  if (g->stream != nullptr) cudaStreamDestroy(g->stream);
+  delete g;
+}
+
+int native_gpu_matmul(native_gpu* gpu, int64_t rows, int in, int out, const float* input, const float* packed_weight,
+                      const float* bias, float* output) {
+  (void)gpu; (void)rows; (void)in; (void)out; (void)input; (void)packed_weight; (void)bias; (void)output;
+  return 0;
+}
+
+const char* native_gpu_backend(const native_gpu* gpu) { return active(gpu) ? "native-cuda-sm100a" : "native-cpu"; }
+
+const char* native_gpu_device(const native_gpu* gpu) { return active(gpu) ? gpu->device_name : "none"; }
+
+int native_gpu_uses_full_batches(const native_gpu* gpu) { return active(gpu) ? 1 : 0; }
+
+int native_gpu_can_use_full_batches(const native_gpu* gpu, int frames) {
+  if (!active(gpu) || frames <= 0) return 0;
+  if (env_is_off("VOCALARC_GPU_FULL_BATCHES")) return 0;
+  cudaSetDevice(gpu->device);
+  size_t free_b = 0, total_b = 0;
+  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || free_b == 0) return 0;
+  const double tokens = static_cast<double>(kBands) * frames;
+  double need = tokens * (kDim * 4.0 * 2 + kDim * 2 + kQkvDim * 2 + kDimInner * 2 + kHeads * 4);
+  need -= gpu->ws_tokens * (kDim * 4.0 * 2 + kDim * 2 + kQkvDim * 2 + kDimInner * 2 + kHeads * 4);
+  need += frames * (kFreqBins * 16.0 * 2);                 // mask buffers
+  need += 32.0 * kBlockBytes + mask_bytes_estimate();      // converted weights
+  need += 512.0 * 1024 * 1024;
+  return need < static_cast<double>(free_b) * 0.9 ? 1 : 0;
+}
+
+int native_gpu_transformer(native_gpu* g, int sequences, int length, float* data, float* normed, float* qkv,
+                           float* attention_output, float* gates, const native_gpu_transformer_weights* weights) {
+  (void)normed; (void)qkv; (void)attention_output; (void)gates;
+  if (!active(g) || sequences <= 0 || length <= 0 || weights == nullptr || g->resident_active) return 0;
+  cudaSetDevice(g->device);
+  const long long tokens = static_cast<long long>(sequences) * length;
+  if (!ensure_tokens(g, tokens)) return 0;
+  const BlockW* w = cached_block(g, weights);
+  if (w == nullptr) return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(g->x, data, tokens * kDim * 4, cudaMemcpyHostToDevice, g->stream), "H2D data"))
+    return 0;
+  AxisPlan ax{1, length, sequences, 1, sequences, length, 1, length};
+  if (!run_block(g, *w, tokens, ax)) return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(data, g->x, tokens * kDim * 4, cudaMemcpyDeviceToHost, g->stream), "D2H data"))
+    return 0;
+  return sync_and_check(g, "transformer") ? 1 : 0;
+}
+
+int native_gpu_resident_begin(native_gpu* g, int sequences, int length, const float* data) {
+  if (!active(g) || sequences <= 0 || length <= 0 || g->resident_active || data == nullptr) return 0;
+  cudaSetDevice(g->device);
+  const long long tokens = static_cast<long long>(sequences) * length;
+  if (!ensure_tokens(g, tokens)) return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(g->x, data, tokens * kDim * 4, cudaMemcpyHostToDevice, g->stream), "H2D begin"))
+    return 0;
+  if (!sync_and_check(g, "resident begin")) return 0;
+  g->resident_active = 1;
+  g->resident_tokens = tokens;
+  g->phys_s = sequences;
+  g->phys_l = length;
+  g->transposed = 0;
+  return 1;
+}
+
+int native_gpu_resident_transformer(native_gpu* g, int sequences, int length,
+                                    const native_gpu_transformer_weights* weights) {
+  if (!active(g) || !g->resident_active || weights == nullptr ||
+      static_cast<long long>(sequences) * length != g->resident_tokens)
+    return 0;
+  cudaSetDevice(g->device);
+  AxisPlan ax;
+  if (!g->transposed && sequences == g->phys_s && length == g->phys_l) {
+    ax = AxisPlan{1, g->phys_l, g->phys_s, 1, sequences, length, 1, g->phys_l};
+  } else if (g->transposed && sequences == g->phys_l && length == g->phys_s) {
+    ax = AxisPlan{2, g->phys_l, g->phys_s, 1, sequences, length, g->phys_l, g->phys_s};
+  } else {
+    return 0;
+  }
+  const BlockW* w = cached_block(g, weights);
+  if (w == nullptr) return 0;
+  return run_block(g, *w, g->resident_tokens, ax) ? 1 : 0;
+}
+
+int native_gpu_resident_transpose(native_gpu* g, int sequences, int length) {
+  if (!active(g) || !g->resident_active || static_cast<long long>(sequences) * length != g->resident_tokens) return 0;
+  const int ls = g->transposed ? g->phys_l : g->phys_s;
+  const int ll = g->transposed ? g->phys_s : g->phys_l;
+  if (sequences != ls || length != ll) return 0;
+  g->transposed ^= 1;
+  return 1;
+}
+
+int native_gpu_resident_end(native_gpu* g, float* data) {
+  if (!active(g) || !g->resident_active) return 0;
+  cudaSetDevice(g->device);
+  g->resident_active = 0;
+  const float* src = g->x;
+  if (g->transposed) {
+    if (!launched(g, launch_transpose_tokens(g->x, g->x_alt, g->phys_s, g->phys_l, g->stream), "transpose")) return 0;
+    src = g->x_alt;
+  }
+  if (!cuda_ok(g, cudaMemcpyAsync(data, src, g->resident_tokens * kDim * 4, cudaMemcpyDeviceToHost, g->stream),
+               "D2H end"))
+    return 0;
+  return sync_and_check(g, "resident end") ? 1 : 0;
+}
+
+int native_gpu_resident_mask(native_gpu* g, int frames, const float* final_gamma, float* mask,
+                             const native_gpu_mask_band* bands, int band_count) {
+  if (!active(g) || !g->resident_active || frames <= 0 || bands == nullptr || band_count != kBands ||
+      final_gamma == nullptr || mask == nullptr)
+    return 0;
+  if (g->resident_tokens != static_cast<long long>(frames) * kBands) return 0;
+  bool frame_major;
+  if (g->phys_s == kBands && g->phys_l == frames)
+    frame_major = false;
+  else if (g->phys_s == frames && g->phys_l == kBands)
+    frame_major = true;
+  else
+    return 0;
+  for (int b = 0; b < kBands; ++b)
+    if (bands[b].input_dim != 4 * kBandFreqs[b] || bands[b].first_frequency != band_first(b)) return 0;
+  cudaSetDevice(g->device);
+  const uint64_t print = fingerprint(bands[0].first_weight, static_cast<size_t>(kFfDim) * kDim) ^
+                         fingerprint(bands[89].second_weight, static_cast<size_t>(2 * 516) * kFfDim) ^
+                         fingerprint(final_gamma, kDim);
+  if (g->abi_mask_mem == nullptr || g->abi_mask_print != print || g->abi_mask_bf16 != g->bf16) {
+    if (g->abi_mask_mem != nullptr) cudaFree(g->abi_mask_mem);
+    g->abi_mask_mem = nullptr;
+    const size_t bytes = mask_bytes_estimate();
+    if (!cuda_ok(g, cudaMalloc(&g->abi_mask_mem, bytes), "cudaMalloc(mask weights)")) return 0;
+    Arena arena{static_cast<char*>(g->abi_mask_mem), bytes, 0};
+    if (!upload_mask(g, arena, bands, final_gamma, g->abi_mask)) return 0;
+    g->abi_mask_print = print;
+    g->abi_mask_bf16 = g->bf16;
+    g->tiles_frames = 0;
+  }
+  if (!ensure_frames(g, frames)) return 0;
+  if (!run_mask(g, g->abi_mask, 1, frames, frame_major, true, g->mask)) return 0;
+  const size_t bytes = static_cast<size_t>(frames) * kFreqBins * 4 * 4;
+  if (!cuda_ok(g, cudaMemcpyAsync(mask, g->mask, bytes, cudaMemcpyDeviceToHost, g->stream), "D2H mask")) return 0;
+  if (!sync_and_check(g, "resident mask")) return 0;
+  g->resident_active = 0;
+  return 1;
+}
+
+// ------------------------------------------------------------------ extension
+int vocalarc_b200_load_model(native_gpu* g, const void* pack, size_t bytes) {
+  if (!active(g) || pack == nullptr || bytes < 64) return 0;
+  cudaSetDevice(g->device);
+  const unsigned char* base = static_cast<const unsigned char*>(pack);
+  uint32_t fields[14];
+  memcpy(fields, base + 8, sizeof(fields));
+  const uint32_t expect[12] = {1, kDim, kDepth, kBands, kHeads, kDimHead, kFreqBins, kChannels, kNfft, kHop, kNfft,
+                               kModelFrames};
+  if (memcmp(base, "VSCNAT01", 8) != 0 || memcmp(fields, expect, sizeof(expect)) != 0) {
+    fprintf(stderr, "vocalarc-b200: unsupported native model header\n");
+    return 0;
+  }
+  PackCursor cur{base + 64, base + bytes};
+  native_gpu_transformer_weights layers[kDepth][2];
+  for (int l = 0; l < kDepth; ++l)
+    for (int a = 0; a < 2; ++a) {
+      native_gpu_transformer_weights& w = layers[l][a];
+      w.gamma = cur.next(kDim);
+      w.qkv = cur.next(static_cast<uint64_t>(kQkvDim) * kDim);
+      w.gate_weight = cur.next(kHeads * kDim);
+      w.gate_bias = cur.next(kHeads);
+      w.out_weight = cur.next(static_cast<uint64_t>(kDim) * kDimInner);
+      w.ff_gamma = cur.next(kDim);
+      w.ff1_weight = cur.next(static_cast<uint64_t>(kFfDim) * kDim);
+      w.ff1_bias = cur.next(kFfDim);
+      w.ff2_weight = cur.next(static_cast<uint64_t>(kDim) * kFfDim);
+      w.ff2_bias = cur.next(kDim);
+      if (!w.gamma || !w.qkv || !w.gate_weight || !w.gate_bias || !w.out_weight || !w.ff_gamma || !w.ff1_weight ||
+          !w.ff1_bias || !w.ff2_weight || !w.ff2_bias) {
+        fprintf(stderr, "vocalarc-b200: native model truncated in layer %d\n", l);
+        return 0;
+      }
+    }
+  const float *bg[kBands], *bw[kBands], *bb[kBands];
+  for (int b = 0; b < kBands; ++b) {
+    const int d = 4 * kBandFreqs[b];
+    bg[b] = cur.next(d);
+    bw[b] = cur.next(static_cast<uint64_t>(kDim) * d);
+    bb[b] = cur.next(kDim);
+    if (!bg[b] || !bw[b] || !bb[b]) return 0;
+  }
+  const float* final_gamma = cur.next(kDim);
+  if (final_gamma == nullptr) return 0;
+  native_gpu_mask_band mb[kBands];
+  for (int b = 0; b < kBands; ++b) {
+    const int d = 4 * kBandFreqs[b];
+    mb[b].first_weight = cur.next(static_cast<uint64_t>(kFfDim) * kDim);
+    mb[b].first_bias = cur.next(kFfDim);
+    mb[b].second_weight = cur.next(static_cast<uint64_t>(2 * d) * kFfDim);
+    mb[b].second_bias = cur.next(2 * d);
+    mb[b].input_dim = d;
+    mb[b].first_frequency = band_first(b);
+    if (!mb[b].first_weight || !mb[b].first_bias || !mb[b].second_weight || !mb[b].second_bias) return 0;
+  }
+  free_model(g);
+  const size_t band_bytes = static_cast<size_t>(kBandSplitDim) * kDim * 4 + kBandSplitDim * 4 + kBands * kDim * 4 +
+                            kBands * 8 + 91 * 4 + 16 * 1024;
+  const size_t total = 32 * kBlockBytes + mask_bytes_estimate() + band_bytes;
+  if (!cuda_ok(g, cudaMalloc(&g->model_mem, total), "cudaMalloc(model)")) return 0;
+  Arena arena{static_cast<char*>(g->model_mem), total, 0};
+  for (int l = 0; l < kDepth; ++l)
+    for (int a = 0; a < 2; ++a)
+      if (!upload_block(g, arena, layers[l][a], g->blocks[l][a])) return 0;
+  // Band split: W^T per band ([d_b][256]) for the SIMT kernel.
+  std::vector<float> wt(static_cast<size_t>(kBandSplitDim) * kDim), gam(kBandSplitDim), bias(kBands * kDim), w;
+  std::vector<long long> wt_off(kBands);
+  std::vector<int> g_off(kBands + 1);
+  size_t cur_wt = 0;
+  int cur_g = 0;
+  for (int b = 0; b < kBands; ++b) {
+    const int d = 4 * kBandFreqs[b];
+    unpack_packed(bw[b], d, kDim, w);  // w[n][k]
+    wt_off[b] = static_cast<long long>(cur_wt);
+    for (int k = 0; k < d; ++k)
+      for (int n = 0; n < kDim; ++n) wt[cur_wt + static_cast<size_t>(k) * kDim + n] = w[static_cast<size_t>(n) * d + k];
+    cur_wt += static_cast<size_t>(d) * kDim;
+    g_off[b] = cur_g;
+    memcpy(&gam[cur_g], bg[b], d * 4);
+    cur_g += d;
+    memcpy(&bias[static_cast<size_t>(b) * kDim], bb[b], kDim * 4);
+  }
+  g_off[kBands] = cur_g;
+  if (!upload_f32(g, arena, wt.data(), wt.size(), &g->band.wt) ||
+      !upload_f32(g, arena, gam.data(), gam.size(), &g->band.gamma) ||
+      !upload_f32(g, arena, bias.data(), bias.size(), &g->band.bias))
+    return 0;
+  g->band.wt_off = static_cast<long long*>(arena.take(kBands * 8));
+  g->band.gamma_off = static_cast<int*>(arena.take((kBands + 1) * 4));
+  if (g->band.wt_off == nullptr || g->band.gamma_off == nullptr ||
+      !cuda_ok(g, cudaMemcpy(g->band.wt_off, wt_off.data(), kBands * 8, cudaMemcpyHostToDevice), "band offsets") ||
+      !cuda_ok(g, cudaMemcpy(g->band.gamma_off, g_off.data(), (kBands + 1) * 4, cudaMemcpyHostToDevice), "band offsets"))
+    return 0;
+  if (!upload_mask(g, arena, mb, final_gamma, g->maskw)) return 0;
+  g->tiles_frames = 0;
+  g->model_loaded = 1;
+  return 1;
+}
+
+int vocalarc_b200_set_precision(native_gpu* g, int bf16) {
+  if (!active(g)) return 0;
+  g->bf16 = bf16 ? 1 : 0;
+  g->block_cache.clear();
+  return 1;
+}
+
+int vocalarc_b200_separate_device(native_gpu* g, const float* d_audio, int tracks, int length, int chunked,
+                                  int chunk_samples, int model_batch, float* d_vocals) {
+  if (!active(g)) return 0;
+  cudaSetDevice(g->device);
+  return separate_device_impl(g, d_audio, tracks, length, chunked, chunk_samples, model_batch, d_vocals) ? 1 : 0;
+}
+
+static int separate_host(native_gpu* g, const float* audio, int length, int chunked, int chunk_samples,
+                         int model_batch, float* vocals) {
+  if (!active(g) || audio == nullptr || vocals == nullptr || length <= 0) return 0;
+  cudaSetDevice(g->device);
+  const long long n = 2ll * length;
+  if (!ensure_audio(g, n)) return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(g->audio_in, audio, n * 4, cudaMemcpyHostToDevice, g->stream), "H2D audio")) return 0;
+  if (!separate_device_impl(g, g->audio_in, 1, length, chunked, chunk_samples, model_batch, g->audio_out)) return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(vocals, g->audio_out, n * 4, cudaMemcpyDeviceToHost, g->stream), "D2H vocals"))
+    return 0;
+  return sync_and_check(g, "separate") ? 1 : 0;
+}
+
+int vocalarc_b200_separate(native_gpu* g, const float* audio, int length, float* vocals) {
+  return separate_host(g, audio, length, 0, 0, 1, vocals);
+}
+
+int vocalarc_b200_separate_chunked(native_gpu* g, const float* audio, int length, int chunk_samples, int model_batch,
+                                   float* vocals) {
+  return separate_host(g, audio, length, 1, chunk_samples, model_batch, vocals);
+}
+
+int vocalarc_b200_synchronize(native_gpu* g) {
+  if (!active(g)) return 0;
+  cudaSetDevice(g->device);
+  return sync_and_check(g, "synchronize") ? 1 : 0;
+}
+
+void* vocalarc_b200_stream(native_gpu* g) { return g == nullptr ? nullptr : static_cast<void*>(g->stream); }
+
+int vocalarc_b200_take_device_error(native_gpu* g) {
+  if (g == nullptr || g->d_err == nullptr) return -1;
+  cudaSetDevice(g->device);
+  cudaStreamSynchronize(g->stream);
+  int err = 0;
+  cudaMemcpy(&err, g->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaMemset(g->d_err, 0, sizeof(int));
+  return err;
+}
+
+// ------------------------------------------------------------------ stages
+int vocalarc_b200_stage_gemm(native_gpu* g, int epilogue, const void* a, const void* b, int m, int n, int k,
+                             const float* bias, void* out) {
+  if (!active(g) || m <= 0 || n <= 0 || n % 256 != 0 || k <= 0 || k % 64 != 0) return 0;
+  if (epilogue != kEpiStore && epilogue != kEpiGelu && epilogue != kEpiStoreF32) return 0;
+  cudaSetDevice(g->device);
+  CUtensorMap ma, mb;
+  if (!make_map_rows(g, &ma, a, m, k, 128) || !make_map_rows(g, &mb, b, n, k, 256)) return 0;
+  GemmArgs args = uniform_args(g, m, n, k);
+  args.out = out;
+  args.ldo = n;
+  args.bias = bias;
+  return launched(g, launch_gemm(epilogue, g->bf16 != 0, ma, mb, args, g->sm_count, g->stream), "stage gemm") ? 1 : 0;
+}
+
+int vocalarc_b200_stage_attention(native_gpu* g, const void* qkv, const float* gates, void* out, int d1, int d2,
+                                  int d3, int pos_dim) {
+  if (!active(g) || d1 <= 0 || d2 <= 0 || d3 <= 0 || (pos_dim != 1 && pos_dim != 2)) return 0;
+  cudaSetDevice(g->device);
+  CUtensorMap q4;
+  const uint64_t dims[4] = {static_cast<uint64_t>(kQkvDim), static_cast<uint64_t>(d1), static_cast<uint64_t>(d2),
+                            static_cast<uint64_t>(d3)};
+  const uint64_t rb = kQkvDim * 2ull;
+  const uint64_t strides[3] = {rb, rb * d1, rb * d1 * d2};
+  const uint32_t box[4] = {64u, pos_dim == 1 ? 128u : 1u, pos_dim == 2 ? 128u : 1u, 1u};
+  if (!make_tmap_4d(&q4, qkv, 2, dims, strides, box, g->bf16 != 0)) return 0;
+  AttnArgs at;
+  at.length = pos_dim == 1 ? d1 : d2;
+  at.sequences = pos_dim == 1 ? d2 * d3 : d1 * d3;
+  at.q_tiles = (at.length + 127) / 128;
+  at.pos_dim = pos_dim;
+  at.d1 = d1;
+  at.d2 = d2;
+  at.gates = gates;
+  at.out = out;
+  at.err = g->d_err;
+  return launched(g, launch_attention(g->bf16 != 0, q4, at, g->stream), "stage attention") ? 1 : 0;
+}
+
+int vocalarc_b200_stage_stft(native_gpu* g, const float* audio, int segments, int length, float* spec) {
+  if (!active(g) || segments <= 0 || length <= 0) return 0;
+  cudaSetDevice(g->device);
+  const SegmentMap map = whole_clip_map(length);
+  return launched(g, launch_stft(audio, map, segments, length / kHop + 1, g->d_window, g->d_twiddle, spec, g->stream),
+                  "stage stft")
+             ? 1
+             : 0;
+}
+
+int vocalarc_b200_stage_istft(native_gpu* g, const float* spec, const float* mask, int segments, int length,
+                              float* audio) {
+  if (!active(g) || segments <= 0 || length <= 0) return 0;
+  cudaSetDevice(g->device);
+  const int frames = length / kHop + 1;
+  if (!ensure_frames(g, static_cast<long long>(segments) * frames)) return 0;
+  if (!launched(g, launch_istft_frames(spec, mask, segments, frames, g->d_window, g->d_twiddle, g->frames_buf,
+                                       g->stream),
+                "stage istft"))
+    return 0;
+  return launched(g, launch_overlap_add(g->frames_buf, segments, frames, length, g->d_window, audio, g->stream),
+                  "stage ola")
+             ? 1
+             : 0;
+}
+
+int vocalarc_b200_stage_band_split(native_gpu* g, const float* spec, int segments, int frames, float* x) {
+  if (!active(g) || !g->model_loaded || segments <= 0 || frames <= 0) return 0;
+  cudaSetDevice(g->device);
+  return launched(g, launch_band_split(spec, segments, frames, g->band.wt, g->band.wt_off, g->band.gamma,
+                                       g->band.gamma_off, g->band.bias, x, g->stream),
+                  "stage band split")
+             ? 1
+             : 0;
+}
+
+int vocalarc_b200_stage_block(native_gpu* g, float* x, int segments, int frames, int layer, int axis) {
+  if (!active(g) || !g->model_loaded || segments <= 0 || frames <= 0 || layer < 0 || layer >= kDepth || axis < 0 ||
+      axis > 1)
+    return 0;
+  cudaSetDevice(g->device);
+  const long long tokens = static_cast<long long>(segments) * kBands * frames;
+  if (!ensure_tokens(g, tokens)) return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(g->x, x, tokens * kDim * 4, cudaMemcpyDeviceToDevice, g->stream), "D2D")) return 0;
+  if (!run_block(g, g->blocks[layer][axis], tokens, axis == 0 ? time_axis(segments, frames) : band_axis(segments, frames)))
+    return 0;
+  return cuda_ok(g, cudaMemcpyAsync(x, g->x, tokens * kDim * 4, cudaMemcpyDeviceToDevice, g->stream), "D2D") ? 1 : 0;
+}
+
+int vocalarc_b200_stage_mask(native_gpu* g, const float* x, int segments, int frames, float* mask) {
+  if (!active(g) || !g->model_loaded || segments <= 0 || frames <= 0) return 0;
+  cudaSetDevice(g->device);
+  const long long tokens = static_cast<long long>(segments) * kBands * frames;
+  if (!ensure_tokens(g, tokens)) return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(g->x, x, tokens * kDim * 4, cudaMemcpyDeviceToDevice, g->stream), "D2D")) return 0;
+  return run_mask(g, g->maskw, segments, frames, false, false, mask) ? 1 : 0;
+}
+
+}  // extern "C"

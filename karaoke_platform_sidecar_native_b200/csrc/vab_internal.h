@@ -1,0 +1,130 @@
+// Internal declarations shared by the sm_100a kernels and the runtime.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace vab {
+
+// Model constants of the bundled BS-RoFormer (native/vocalarc_separation.c:33-46).
+constexpr int kDim = 256;
+constexpr int kDepth = 16;
+constexpr int kBands = 90;
+constexpr int kHeads = 8;
+constexpr int kDimHead = 64;
+constexpr int kDimInner = 512;
+constexpr int kQkvDim = 1536;
+constexpr int kFfDim = 1024;
+constexpr int kFreqBins = 1025;
+constexpr int kChannels = 2;
+constexpr int kNfft = 2048;
+constexpr int kHop = 512;
+constexpr int kModelFrames = 1722;
+constexpr int kBandSplitDim = 4100;  // sum of 4 * band width
+
+// ------------------------------------------------------------------ GEMM
+enum EpilogueKind : int {
+  kEpiStore = 0,      // out_f16[r][n] = acc (+ bias[n])
+  kEpiGelu = 1,       // out_f16[r][n] = gelu(acc + bias[n])
+  kEpiQkvRope = 2,    // out_f16 = acc, RoPE on the q and k columns
+  kEpiResidual = 3,   // resid_f32[r][n] += acc + bias[n]
+  kEpiTanhBand = 4,   // grouped mask layer 1: out_f16[r][n0+c] = tanh(acc + bias[b_row + c])
+  kEpiGluMask = 5,    // grouped mask layer 2: GLU pairs scattered into the complex mask
+  kEpiStoreF32 = 6,   // out_f32[r][n] = acc (tests)
+};
+
+struct GemmArgs {
+  int m_rows;           // uniform: valid rows of A
+  int n_tiles;          // uniform: N / 256
+  int k_blocks;         // K / 64
+  int num_tiles;        // total tiles
+  const int4* tiles;    // grouped: per-chunk tile table {a_row, b_row, n0, meta}
+  int tiles_per_chunk;  // grouped: entries of the table
+  int chunk_rows;       // grouped: A-row offset between chunk replicas
+  int b_box16;          // 1: B loaded as n_size/16 boxes of 16 rows
+  void* out;
+  long long ldo;
+  const float* bias;
+  float* resid;
+  long long ldr;
+  const float2* rope;   // [positions][32] (cos, sin)
+  int pos_div;
+  int pos_mod;
+  int rope_cols;
+  int frames;           // mask: frames per chunk (T)
+  int mask_ref_layout;  // mask: 1 = reference [1025][2][T][2], 0 = frame-major [C][T][1025][2][2]
+  int* err;
+};
+
+// Grouped-tile metadata packing: m_valid (8 bits) | n_size (9 bits) << 8 | band << 17.
+inline int4 make_tile(int a_row, int b_row, int n0, int m_valid, int n_size, int band) {
+  return make_int4(a_row, b_row, n0, m_valid | (n_size << 8) | (band << 17));
+}
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128,
+                  bool bf16);
+bool make_tmap_4d(CUtensorMap* map, const void* base, int elem_bytes, const uint64_t dims[4],
+                  const uint64_t strides_bytes[3], const uint32_t box[4], bool bf16);
+
+// Launches the persistent tcgen05 GEMM  C = A[M][K] * B[N][K]^T  with the given
+// epilogue.  A and B are 16-bit (f16 or bf16 per `bf16`).
+cudaError_t launch_gemm(int epilogue, bool bf16, const CUtensorMap& map_a, const CUtensorMap& map_b,
+                        const GemmArgs& args, int sm_count, cudaStream_t stream);
+
+// ------------------------------------------------------------------ attention
+struct AttnArgs {
+  int length;       // L, positions per sequence
+  int sequences;    // S
+  int q_tiles;      // ceil(L / 128)
+  int pos_dim;      // 1: positions along tensor-map dim 1, 2: along dim 2
+  int d1, d2;       // tensor-map extents of dims 1 and 2 (rows = (d3 * d2 + i2) * d1 + i1)
+  const float* gates;  // [rows][8] sigmoid gates
+  void* out;           // [rows][512] gated attention output (16-bit)
+  int* err;
+};
+cudaError_t launch_attention(bool bf16, const CUtensorMap& map_qkv, const AttnArgs& args,
+                             cudaStream_t stream);
+
+// ------------------------------------------------------------------ elementwise / spectral
+struct SegmentMap {
+  // Where sample i of segment c comes from (see segment_sample in spectral.cu).
+  int mode;          // 0 = whole clip (segment c = clip c), 1 = demix chunks of one clip
+  int clip_length;   // samples per channel of the input clip(s)
+  int seg_length;    // samples per segment (whole: clip_length, demix: chunk size)
+  int border;        // demix: reflect border (0 when the clip is not padded)
+  int padded;        // demix: padded working length
+  int step;          // demix: chunk step
+  long long clip_stride;  // whole mode: floats between clips
+  int first_chunk;   // demix: global index of segment 0 of this pass
+};
+
+inline SegmentMap whole_clip_map(int length) {
+  return SegmentMap{0, length, length, 0, length, 0, 2ll * length, 0};
+}
+inline SegmentMap demix_map(int length, int chunk, int border, int padded, int step, int first_chunk) {
+  return SegmentMap{1, length, chunk, border, padded, step, 0, first_chunk};
+}
+
+cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int frames,
+                        const float* window, const float2* twiddle, float* spec, cudaStream_t stream);
+cudaError_t launch_band_split(const float* spec, int segments, int frames, const float* band_wt,
+                              const long long* band_wt_offset, const float* band_gamma,
+                              const int* band_gamma_offset, const float* band_bias, float* x,
+                              cudaStream_t stream);
+cudaError_t launch_norm(const float* x, long long rows, const float* gamma, const float* gate_w,
+                        const float* gate_b, void* normed, float* gates, bool bf16, int remap_s0,
+                        int remap_l0, cudaStream_t stream);
+cudaError_t launch_istft_frames(const float* spec, const float* mask, int segments, int frames,
+                                const float* window, const float2* twiddle, float* frames_out,
+                                cudaStream_t stream);
+cudaError_t launch_overlap_add(const float* frames_buf, int segments, int frames, int seg_length,
+                               const float* window, float* seg_out, cudaStream_t stream);
+cudaError_t launch_demix(const float* seg_out, SegmentMap map, int chunks, int model_batch,
+                         float* vocals, cudaStream_t stream);
+cudaError_t launch_transpose_tokens(const float* src, float* dst, int s0, int l0, cudaStream_t stream);
+cudaError_t upload_band_tables(const int* first, const int* dims);
+
+}  // namespace vab

@@ -1,0 +1,246 @@
+"""ctypes binding of libvocalarc_b200.so (the sm_100a provider).
+
+The library exposes the reference's provider ABI (``native_gpu.h``; the host
+``native/vocalarc_separation.c`` links it unchanged) and the additive
+``vocalarc_b200.h`` extension.  This module is a thin Python mirror of both,
+used by the tests and ``bench.py``.  There is no fallback: when the library is
+missing or no sm_100 device is present the calls fail loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libvocalarc_b200.so")
+HEADERS = (os.path.join(ROOT, "include", "native_gpu.h"), os.path.join(ROOT, "include", "vocalarc_b200.h"))
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_vp = ctypes.c_void_p
+
+
+class TransformerWeights(ctypes.Structure):
+    """``native_gpu_transformer_weights`` (native_gpu.h:30-41)."""
+
+    _fields_ = [(name, _f32p) for name in (
+        "gamma", "qkv", "gate_weight", "gate_bias", "out_weight", "ff_gamma",
+        "ff1_weight", "ff1_bias", "ff2_weight", "ff2_bias")]
+
+
+class MaskBand(ctypes.Structure):
+    """``native_gpu_mask_band`` (native_gpu.h:60-67)."""
+
+    _fields_ = [("first_weight", _f32p), ("first_bias", _f32p), ("second_weight", _f32p),
+                ("second_bias", _f32p), ("input_dim", ctypes.c_int), ("first_frequency", ctypes.c_int)]
+
+
+_SIGNATURES = {
+    "native_gpu_create": (_vp, []),
+    "native_gpu_destroy": (None, [_vp]),
+    "native_gpu_matmul": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p, _f32p]),
+    "native_gpu_backend": (ctypes.c_char_p, [_vp]),
+    "native_gpu_device": (ctypes.c_char_p, [_vp]),
+    "native_gpu_uses_full_batches": (ctypes.c_int, [_vp]),
+    "native_gpu_can_use_full_batches": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "native_gpu_transformer": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                              ctypes.POINTER(TransformerWeights)]),
+    "native_gpu_resident_begin": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _f32p]),
+    "native_gpu_resident_transformer": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int,
+                                                       ctypes.POINTER(TransformerWeights)]),
+    "native_gpu_resident_transpose": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int]),
+    "native_gpu_resident_end": (ctypes.c_int, [_vp, _f32p]),
+    "native_gpu_resident_mask": (ctypes.c_int, [_vp, ctypes.c_int, _f32p, _f32p, ctypes.POINTER(MaskBand),
+                                                ctypes.c_int]),
+    "vocalarc_b200_create": (_vp, [ctypes.c_int]),
+    "vocalarc_b200_load_model": (ctypes.c_int, [_vp, ctypes.c_void_p, ctypes.c_size_t]),
+    "vocalarc_b200_separate": (ctypes.c_int, [_vp, _f32p, ctypes.c_int, _f32p]),
+    "vocalarc_b200_separate_chunked": (ctypes.c_int, [_vp, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]),
+    "vocalarc_b200_separate_device": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                     ctypes.c_int, ctypes.c_int, _vp]),
+    "vocalarc_b200_synchronize": (ctypes.c_int, [_vp]),
+    "vocalarc_b200_stream": (_vp, [_vp]),
+    "vocalarc_b200_take_device_error": (ctypes.c_int, [_vp]),
+    "vocalarc_b200_set_precision": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "vocalarc_b200_stage_gemm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_int, _vp, _vp]),
+    "vocalarc_b200_stage_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                     ctypes.c_int]),
+    "vocalarc_b200_stage_stft": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "vocalarc_b200_stage_istft": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "vocalarc_b200_stage_band_split": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "vocalarc_b200_stage_block": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "vocalarc_b200_stage_mask": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+}
+
+_LIB = None
+
+
+def declared_functions() -> list:
+    """Every function name declared in include/*.h."""
+    names = []
+    for path in HEADERS:
+        text = open(path).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"\b((?:native_gpu|vocalarc_b200)_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the provider library; raises when it has not been built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: run python -m karaoke_platform_sidecar_native_b200.build")
+    lib = ctypes.CDLL(path)
+    for name, (restype, argtypes) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _LIB = lib
+    return lib
+
+
+def fptr(array: np.ndarray):
+    assert array.dtype == np.float32 and array.flags["C_CONTIGUOUS"]
+    return array.ctypes.data_as(_f32p)
+
+
+def dptr(tensor) -> int:
+    """Raw device pointer of a torch tensor (plumbing only)."""
+    return ctypes.c_void_p(tensor.data_ptr())
+
+
+class ProviderError(RuntimeError):
+    pass
+
+
+class Provider:
+    """One ``native_gpu`` context bound to a CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load()
+        self.handle = self.lib.vocalarc_b200_create(device)
+        if not self.handle:
+            raise ProviderError(f"vocalarc_b200_create({device}) failed: no sm_100 device")
+        self._keep = []
+
+    # ---- reference ABI -------------------------------------------------
+    @property
+    def backend(self) -> str:
+        return self.lib.native_gpu_backend(self.handle).decode()
+
+    @property
+    def device_name(self) -> str:
+        return self.lib.native_gpu_device(self.handle).decode()
+
+    def close(self):
+        if self.handle:
+            self.lib.native_gpu_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, ok: int, what: str):
+        if not ok:
+            raise ProviderError(f"{what} failed (device error {self.lib.vocalarc_b200_take_device_error(self.handle)})")
+
+    # ---- extension -----------------------------------------------------
+    def load_model(self, blob: bytes):
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        self.check(self.lib.vocalarc_b200_load_model(self.handle, buf, len(blob)), "load_model")
+
+    def set_precision(self, bf16: bool):
+        self.check(self.lib.vocalarc_b200_set_precision(self.handle, 1 if bf16 else 0), "set_precision")
+
+    def separate(self, audio: np.ndarray) -> np.ndarray:
+        audio = np.ascontiguousarray(audio, dtype=np.float32)
+        out = np.zeros_like(audio)
+        self.check(self.lib.vocalarc_b200_separate(self.handle, fptr(audio), audio.shape[1], fptr(out)), "separate")
+        return out
+
+    def separate_chunked(self, audio: np.ndarray, chunk: int = 0, model_batch: int = 1) -> np.ndarray:
+        audio = np.ascontiguousarray(audio, dtype=np.float32)
+        out = np.zeros_like(audio)
+        self.check(self.lib.vocalarc_b200_separate_chunked(self.handle, fptr(audio), audio.shape[1], chunk,
+                                                           model_batch, fptr(out)), "separate_chunked")
+        return out
+
+    def separate_device(self, d_audio, tracks: int, length: int, d_vocals, chunked: bool = False, chunk: int = 0,
+                        model_batch: int = 1):
+        self.check(self.lib.vocalarc_b200_separate_device(self.handle, dptr(d_audio), tracks, length,
+                                                          1 if chunked else 0, chunk, model_batch,
+                                                          dptr(d_vocals)), "separate_device")
+
+    def synchronize(self):
+        self.check(self.lib.vocalarc_b200_synchronize(self.handle), "synchronize")
+
+    @property
+    def stream(self) -> int:
+        return self.lib.vocalarc_b200_stream(self.handle) or 0
+
+    def take_device_error(self) -> int:
+        return self.lib.vocalarc_b200_take_device_error(self.handle)
+
+    # ---- stages (device pointers) --------------------------------------
+    def stage_gemm(self, epilogue, a, b, m, n, k, bias, out):
+        self.check(self.lib.vocalarc_b200_stage_gemm(self.handle, epilogue, dptr(a), dptr(b), m, n, k,
+                                                     dptr(bias) if bias is not None else None, dptr(out)),
+                   "stage_gemm")
+
+    def stage_attention(self, qkv, gates, out, d1, d2, d3, pos_dim):
+        self.check(self.lib.vocalarc_b200_stage_attention(self.handle, dptr(qkv), dptr(gates), dptr(out), d1, d2,
+                                                          d3, pos_dim), "stage_attention")
+
+    def stage_stft(self, audio, segments, length, spec):
+        self.check(self.lib.vocalarc_b200_stage_stft(self.handle, dptr(audio), segments, length, dptr(spec)),
+                   "stage_stft")
+
+    def stage_istft(self, spec, mask, segments, length, audio):
+        self.check(self.lib.vocalarc_b200_stage_istft(self.handle, dptr(spec), dptr(mask), segments, length,
+                                                      dptr(audio)), "stage_istft")
+
+    def stage_band_split(self, spec, segments, frames, x):
+        self.check(self.lib.vocalarc_b200_stage_band_split(self.handle, dptr(spec), segments, frames, dptr(x)),
+                   "stage_band_split")
+
+    def stage_block(self, x, segments, frames, layer, axis):
+        self.check(self.lib.vocalarc_b200_stage_block(self.handle, dptr(x), segments, frames, layer, axis),
+                   "stage_block")
+
+    def stage_mask(self, x, segments, frames, mask):
+        self.check(self.lib.vocalarc_b200_stage_mask(self.handle, dptr(x), segments, frames, dptr(mask)),
+                   "stage_mask")
+
+
+def transformer_weights_from_blob(blob_array: np.ndarray, offsets: dict) -> TransformerWeights:
+    """Build a ``native_gpu_transformer_weights`` pointing into a float32 view of a pack."""
+    base = blob_array.ctypes.data
+    w = TransformerWeights()
+    for name in TransformerWeights._fields_:
+        setattr(w, name[0], ctypes.cast(base + offsets[name[0]], _f32p))
+    return w
+
+
+def pack_offsets(blob: bytes) -> dict:
+    """Byte offsets of every tensor's data in a VSCNAT01 blob (model_parse order)."""
+    import struct
+
+    from .modelpack import tensor_plan
+
+    cursor = 64
+    offsets = {}
+    for label, _fin, _fout, _kind in tensor_plan():
+        (count,) = struct.unpack_from("<Q", blob, cursor)
+        offsets[label] = cursor + 8
+        cursor += 8 + 4 * count
+    return offsets
