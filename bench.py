@@ -1,0 +1,414 @@
+#!/usr/bin/env python3
+"""Benchmark: audio-seconds separated per second on B200 (BS-RoFormer forward).
+
+Workload (N=1): BASELINE config 2 -- the bundled-layout model (synthetic
+weights, seed 0; the real pack is a missing Git-LFS object) on a 240 s stereo
+44.1 kHz synthetic mix (seed 1: tones redrawn every 0.5 s, pink noise, 120 BPM
+clicks), separated in chunked mode: 27 chunks of 881,559 samples (T = 1,722
+frames), overlap 2, linear fade (Separator::demix semantics).  One step = one
+full separation of that track.  With N GPUs each rank separates its own
+240 s track (seed 1 + rank): weak scaling, no data-path collective.
+
+* ``value``: audio-s/s with the input resident in HBM (device pointers),
+  timed with CUDA events on the provider stream, max over ranks.
+* ``e2e``: the same through the C-ABI call ``vocalarc_b200_separate_chunked``
+  with pinned host buffers (H2D of the mix and D2H of the vocals inside).
+* ``roofline``: the dominant kernel from the live launch trace of the timed
+  steps; achieved = algorithmic FLOPs (or bytes) per launch / mean launch time.
+* ``cpu_baseline``: the unchanged reference CPU executable (built by
+  oracle/Makefile) on a bounded sample on this host's cores.
+
+``--impl reference`` times the reference's own CPU implementation (the same
+executable) on bounded samples of the workload and prints the same JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from karaoke_platform_sidecar_native_b200 import fixtures, modelpack  # noqa: E402
+
+METRIC = "audio-seconds separated per second (BS-RoFormer vocal separation, 240 s mix, chunked)"
+UNIT = "audio_s/s"
+REF_EXE = os.path.join(ROOT, "oracle", "_ref", "vocalarc-separation")
+CHUNK = 881_559
+FRAMES = CHUNK // 512 + 1
+BAND_DIMS_SUM = sum(modelpack.BAND_DIMS)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return {"hbm_gbs": p["hbm_gbs"], "tflops": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "source": "measured (MEASURED_PEAKS.json; sustained bf16 for kernels inside a long step)"}
+    return {"hbm_gbs": 6650.0, "tflops": 1400.0, "source": "fallback (6.65 TB/s, 1.4 PFLOP/s sustained)"}
+
+
+def chunk_count(length):
+    step = CHUNK // 2
+    border = CHUNK - step
+    padded = length + 2 * border if length > 2 * border else length
+    return (padded + step - 1) // step
+
+
+def kernel_work(name, chunks_per_launch):
+    """Algorithmic work of one launch: (kind, amount) with kind 'flop' or 'byte'."""
+    c, t = chunks_per_launch, FRAMES
+    tokens = c * 90 * t
+    flops = {
+        "qkv gemm": 2 * tokens * 256 * 1536,
+        "out gemm": 2 * tokens * 512 * 256,
+        "ff1 gemm": 2 * tokens * 256 * 1024,
+        "ff2 gemm": 2 * tokens * 1024 * 256,
+        "attention (L>128)": 4 * 64 * 8 * (c * 90) * t * t,
+        "attention (L<=128)": 4 * 64 * 8 * (c * t) * 90 * 90,
+        "mask gemm 1": 2 * tokens * 256 * 1024,
+        "mask gemm 2": 2 * c * t * 2 * BAND_DIMS_SUM * 1024,
+    }
+    bytes_ = {
+        "norm+gates": tokens * (256 * 4 + 256 * 2 + 8 * 4),
+        "ff norm": tokens * (256 * 4 + 256 * 2),
+        "final norm": tokens * (256 * 4 + 256 * 2),
+        "stft": c * (2 * CHUNK * 4 + t * 1025 * 16),
+        "band split": c * t * (1025 * 16 + 90 * 256 * 4),
+        "istft": c * t * (2 * 1025 * 16 + 2 * 2048 * 4),
+        "overlap-add": c * (t * 2 * 2048 * 4 + 2 * CHUNK * 4),
+    }
+    if name in flops:
+        return "flop", float(flops[name])
+    if name in bytes_:
+        return "byte", float(bytes_[name])
+    return None, 0.0
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_ids):
+        self.bus_ids = {b.lower()[-12:] for b in bus_ids}
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10 or parts[1].lower()[-12:] not in self.bus_ids:
+                continue
+            try:
+                sm.append(float(parts[2]))
+                smax.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[6:10]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_cpu_run(pack_path, clips, threads, warmup=1):
+    """Run the reference executable over JSONL on the given clips.
+
+    Returns [(audio_seconds, inference_ms, wall_s)] for the clips after warmup.
+    """
+    results = []
+    with tempfile.TemporaryDirectory() as tmp:
+        proc = subprocess.Popen([REF_EXE, "--model", pack_path, "--threads", str(threads)], stdin=subprocess.PIPE,
+                                stdout=subprocess.PIPE, text=True)
+
+        def request(obj):
+            proc.stdin.write(json.dumps(obj) + "\n")
+            proc.stdin.flush()
+            return json.loads(proc.stdout.readline())
+
+        assert request({"id": 0, "type": "load"})["ok"]
+        for i, audio in enumerate(clips):
+            wav = os.path.join(tmp, f"in{i}.wav")
+            fixtures.write_wav_f32(wav, audio)
+            t0 = time.perf_counter()
+            reply = request({"id": i + 1, "type": "separate", "inputPath": wav,
+                             "vocalsPath": os.path.join(tmp, "v.wav")})
+            wall = time.perf_counter() - t0
+            assert reply["ok"], reply
+            if i >= warmup:
+                results.append((audio.shape[1] / 44100.0, reply["inferenceMs"], wall))
+        request({"id": 99, "type": "shutdown"})
+        proc.wait(timeout=60)
+    return results
+
+
+def cpu_baseline(sample_seconds):
+    if not os.path.exists(REF_EXE):
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
+                "sample": "reference executable not built (make -C oracle ref)"}
+    threads = os.cpu_count() or 1
+    pack = modelpack.pack_path(modelpack.BENCH_RECIPE)
+    audio = fixtures.long_mix(240.0, seed=1)
+    n = int(sample_seconds * 44100)
+    clips = [audio[:, :n // 4], audio[:, n: 2 * n]]     # short warm-up request, then the timed sample
+    res = reference_cpu_run(pack, clips, threads, warmup=1)
+    secs = sum(r[0] for r in res)
+    ms = sum(r[1] for r in res)
+    return {"value": secs / (ms / 1000.0), "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": (f"{sample_seconds:g} s excerpt of the 240 s mix through the unchanged reference CPU "
+                       f"executable (whole-clip forward, T={n // 512 + 1}); the workload's 20 s chunks "
+                       f"(T={FRAMES}) cost more per audio second (attention is O(T^2)), so this overstates "
+                       f"the CPU on the workload"),
+            "inference_ms": ms}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    pack = modelpack.pack_path(modelpack.BENCH_RECIPE)
+    audio = fixtures.long_mix(240.0, seed=1)
+    n = int(args.reference_sample_seconds * 44100)
+    clips = [audio[:, (i % 200) * n:(i % 200 + 1) * n] for i in range(args.warmup + args.steps)]
+    res = reference_cpu_run(pack, clips, threads, warmup=args.warmup)
+    secs = sum(r[0] for r in res)
+    ms = sum(r[1] for r in res)
+    wall = sum(r[2] for r in res)
+    value = secs / (ms / 1000.0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / max(1, len(res)), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2: 240 s mix, bundled-layout model (synthetic weights)",
+                   "sample_per_step": f"{args.reference_sample_seconds:g} s excerpt, whole-clip forward"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{args.reference_sample_seconds:g} s excerpts of the 240 s mix per step"},
+        "e2e": {"value": secs / wall, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def traffic_per_launch(kernel):
+    """DRAM bytes per launch of `kernel` at the bench's shape, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith(kernel + "\t"):
+            try:
+                return float(line.split("\t")[1])
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=5)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    parser.add_argument("--seconds", type=float, default=240.0)
+    parser.add_argument("--cpu-sample-seconds", type=float, default=2.0)
+    parser.add_argument("--reference-sample-seconds", type=float, default=1.0)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--precision", default="fp16", choices=("fp16", "bf16"))
+    args = parser.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    from karaoke_platform_sidecar_native_b200 import native
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+
+    provider = native.Provider(local_rank)
+    if args.precision == "bf16":
+        provider.set_precision(True)
+    provider.load_model(modelpack.synthetic_pack(**modelpack.BENCH_RECIPE))
+    length = int(args.seconds * 44100)
+    audio = fixtures.long_mix(args.seconds, seed=1 + rank)
+    d_audio = torch.from_numpy(audio).cuda()
+    d_vocals = torch.empty_like(d_audio)
+    stream = torch.cuda.ExternalStream(provider.stream)
+
+    def step():
+        provider.separate_device(d_audio, 1, length, d_vocals, chunked=True, chunk=CHUNK, model_batch=1)
+
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step()
+    provider.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timed region
+    bus = torch.cuda.get_device_properties(local_rank).pci_bus_id if hasattr(
+        torch.cuda.get_device_properties(local_rank), "pci_bus_id") else ""
+    sampler = ClockSampler([bus] if bus else [])
+    barrier()
+    torch.cuda.synchronize()
+    provider.synchronize()
+    sampler.start()
+    launches0 = provider.launch_count
+    provider.trace_begin()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    trace = provider.trace_end()
+    provider.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    launches = provider.launch_count - launches0
+    elapsed_ms = start.elapsed_time(stop)
+    t = torch.tensor([elapsed_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    value = world * args.seconds * args.steps / (elapsed_ms / 1000.0)
+
+    # ---- end to end through the C-ABI with pinned host buffers
+    host_in = torch.from_numpy(audio).pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    in_np = host_in.numpy()
+    out_np = host_out.numpy()
+    lib = provider.lib
+    e2e_steps = max(1, min(args.steps, 3))
+    barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_stop = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        ok = lib.vocalarc_b200_separate_chunked(provider.handle, native.fptr(in_np), length, CHUNK, 1,
+                                                native.fptr(out_np))
+        if not ok:
+            raise RuntimeError("vocalarc_b200_separate_chunked failed")
+    e_stop.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e_start.elapsed_time(e_stop)
+    t = torch.tensor([e_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e_ms = float(t.item())
+    e2e_value = world * args.seconds * e2e_steps / (e_ms / 1000.0)
+    if not np.isfinite(out_np).all():
+        raise RuntimeError("non-finite vocals")
+
+    if rank == 0:
+        peaks = load_peaks()
+        chunks = chunk_count(length)
+        kernels = []
+        for name, (count, ms) in sorted(trace.items(), key=lambda kv: -kv[1][1]):
+            kind, work = kernel_work(name, chunks)
+            per_launch_ms = ms / max(1, count)
+            entry = {"kernel": name, "launches": count, "total_ms": round(ms, 3),
+                     "share": round(ms / max(1e-9, sum(v[1] for v in trace.values())), 4)}
+            if kind == "flop":
+                ach = work / (per_launch_ms / 1000.0) / 1e12
+                entry.update(achieved_tflops=round(ach, 1), frac=round(ach / peaks["tflops"], 3))
+            elif kind == "byte":
+                ach = work / (per_launch_ms / 1000.0) / 1e9
+                entry.update(achieved_gbs=round(ach, 1), frac=round(ach / peaks["hbm_gbs"], 3))
+            kernels.append(entry)
+        dominant = next((k for k in kernels if "frac" in k), None)
+        roofline = None
+        if dominant is not None:
+            kind, work = kernel_work(dominant["kernel"], chunks)
+            per_launch_s = dominant["total_ms"] / dominant["launches"] / 1000.0
+            if kind == "flop":
+                ach = work / per_launch_s / 1e12
+                roofline = {"kernel": dominant["kernel"], "bound": "tensor", "achieved": round(ach, 1),
+                            "peak": peaks["tflops"], "unit": "TFLOP/s", "frac": round(ach / peaks["tflops"], 4),
+                            "traffic": traffic_per_launch(dominant["kernel"]), "peak_source": peaks["source"],
+                            "work_per_launch": work}
+            else:
+                ach = work / per_launch_s / 1e9
+                roofline = {"kernel": dominant["kernel"], "bound": "hbm", "achieved": round(ach, 1),
+                            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4),
+                            "traffic": traffic_per_launch(dominant["kernel"]), "peak_source": peaks["source"],
+                            "work_per_launch": work}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(args.cpu_sample_seconds)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+            "config": {"workload": "cfg2: 240 s stereo 44.1 kHz mix (seed 1 + rank), chunked demix, "
+                                   f"{chunks} chunks x {CHUNK} samples (T={FRAMES}), bundled-layout model with "
+                                   "synthetic N(0,0.02) weights",
+                       "chunks_per_step": chunks, "audio_seconds_per_step_per_gpu": args.seconds,
+                       "l2": "inputs and workspace (~1 GB per chunk) far larger than the 126 MB L2; no flush",
+                       "parallelism": f"weak: one track per GPU x{world}"},
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(audio.nbytes),
+                    "d2h_bytes_per_step": int(audio.nbytes), "steps": e2e_steps,
+                    "api": "vocalarc_b200_separate_chunked (C-ABI, pinned host buffers)"},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    provider.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

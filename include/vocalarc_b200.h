@@ -55,6 +55,17 @@ int vocalarc_b200_take_device_error(native_gpu *gpu);
 /* 0 = fp16 operands (default), 1 = bf16 operands; both accumulate in fp32. */
 int vocalarc_b200_set_precision(native_gpu *gpu, int bf16);
 
+/* Number of kernels this provider has launched (all streams it owns). */
+long long vocalarc_b200_launch_count(const native_gpu *gpu);
+/* Launch trace: after trace_begin every launch records a CUDA event on the
+   provider stream; trace_end synchronises and writes one line per kernel,
+   "name<TAB>launches<TAB>total_ms", where a launch's time is the gap to the
+   previous event (the stream runs launches back to back). trace_mark adds a
+   named boundary, e.g. after a copy the caller enqueued on the stream. */
+int vocalarc_b200_trace_begin(native_gpu *gpu);
+int vocalarc_b200_trace_mark(native_gpu *gpu, const char *what);
+int vocalarc_b200_trace_end(native_gpu *gpu, char *out, int capacity);
+
 /* ---- stage entry points (device pointers, provider stream) used by the
    parity tests to check each kernel against the CPU oracle ---- */
 

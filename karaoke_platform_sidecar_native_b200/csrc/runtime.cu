@@ -202,6 +202,12 @@ struct native_gpu {
   long long resident_tokens = 0;
   int phys_s = 0, phys_l = 0;   // layout of the device buffer: [phys_s][phys_l]
   int transposed = 0;           // logical layout = [phys_l][phys_s] when set
+  // launch trace: one event after every launch on the provider stream
+  long long launches = 0;
+  int trace = 0;
+  cudaEvent_t trace_base = nullptr;
+  std::vector<cudaEvent_t> event_pool;
+  std::vector<std::pair<const char*, cudaEvent_t>> trace_entries;
 };
 
 namespace {
@@ -213,8 +219,22 @@ bool cuda_ok(native_gpu* g, cudaError_t e, const char* what) {
   return false;
 }
 
+void trace_mark(native_gpu* g, const char* what) {
+  const size_t used = g->trace_entries.size();
+  if (used == g->event_pool.size()) {
+    cudaEvent_t ev = nullptr;
+    if (cudaEventCreate(&ev) != cudaSuccess) return;
+    g->event_pool.push_back(ev);
+  }
+  cudaEvent_t ev = g->event_pool[used];
+  cudaEventRecord(ev, g->stream);
+  g->trace_entries.emplace_back(what, ev);
+}
+
 bool launched(native_gpu* g, cudaError_t e, const char* what) {
   if (!cuda_ok(g, e, what)) return false;
+  ++g->launches;
+  if (g->trace) trace_mark(g, what);
   if (g->debug) {
     if (!cuda_ok(g, cudaStreamSynchronize(g->stream), what)) return false;
     int err = 0;
@@ -483,7 +503,8 @@ bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan&
   at.gates = g->gates;
   at.out = g->attn;
   at.err = g->d_err;
-  if (!launched(g, launch_attention(bf, q4, at, g->stream), "attention")) return false;
+  if (!launched(g, launch_attention(bf, q4, at, g->stream), ax.length <= 128 ? "attention (L<=128)" : "attention (L>128)"))
+    return false;
 
   if (!make_map_rows(g, &a, g->attn, tokens, kDimInner, 128)) return false;
   args = uniform_args(g, tokens, kDim, kDimInner);
@@ -763,6 +784,8 @@ void native_gpu_destroy(native_gpu* g) {
     if (p != nullptr) cudaFree(p);
   for (auto& e : g->block_cache) cudaFree(e.mem);
   free_model(g);
+  for (cudaEvent_t ev : g->event_pool) cudaEventDestroy(ev);
+  if (g->trace_base != nullptr) cudaEventDestroy(g->trace_base);
   if (g->stream != nullptr) cudaStreamDestroy(g->stream);
   delete g;
 }
@@ -1061,6 +1084,59 @@ int vocalarc_b200_take_device_error(native_gpu* g) {
   cudaMemcpy(&err, g->d_err, sizeof(int), cudaMemcpyDeviceToHost);
   cudaMemset(g->d_err, 0, sizeof(int));
   return err;
+}
+
+// ------------------------------------------------------------------ trace
+long long vocalarc_b200_launch_count(const native_gpu* g) { return g == nullptr ? 0 : g->launches; }
+
+int vocalarc_b200_trace_begin(native_gpu* g) {
+  if (!active(g)) return 0;
+  cudaSetDevice(g->device);
+  if (g->trace_base == nullptr && cudaEventCreate(&g->trace_base) != cudaSuccess) return 0;
+  g->trace_entries.clear();
+  cudaEventRecord(g->trace_base, g->stream);
+  g->trace = 1;
+  return 1;
+}
+
+int vocalarc_b200_trace_mark(native_gpu* g, const char* what) {
+  if (!active(g) || !g->trace) return 0;
+  trace_mark(g, what);
+  return 1;
+}
+
+int vocalarc_b200_trace_end(native_gpu* g, char* out, int capacity) {
+  if (!active(g) || !g->trace || out == nullptr || capacity <= 0) return 0;
+  cudaSetDevice(g->device);
+  g->trace = 0;
+  if (!cuda_ok(g, cudaStreamSynchronize(g->stream), "trace")) return 0;
+  std::vector<std::string> names;
+  std::vector<double> ms;
+  std::vector<long long> counts;
+  cudaEvent_t prev = g->trace_base;
+  for (auto& entry : g->trace_entries) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, prev, entry.second);
+    prev = entry.second;
+    size_t i = 0;
+    while (i < names.size() && names[i] != entry.first) ++i;
+    if (i == names.size()) {
+      names.emplace_back(entry.first);
+      ms.push_back(0.0);
+      counts.push_back(0);
+    }
+    ms[i] += t;
+    counts[i] += 1;
+  }
+  g->trace_entries.clear();
+  std::string text;
+  char line[256];
+  for (size_t i = 0; i < names.size(); ++i) {
+    snprintf(line, sizeof(line), "%s\t%lld\t%.6f\n", names[i].c_str(), counts[i], ms[i]);
+    text += line;
+  }
+  snprintf(out, static_cast<size_t>(capacity), "%s", text.c_str());
+  return 1;
 }
 
 // ------------------------------------------------------------------ stages

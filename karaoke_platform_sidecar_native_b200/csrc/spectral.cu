@@ -306,8 +306,11 @@ __global__ void __launch_bounds__(256) overlap_add_kernel(const float* __restric
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= seg_length) return;
   const int cc = blockIdx.y;  // segment * 2 + channel
-  const int f_hi = min(frames - 1, (s + kNfft / 2) / kHop);
-  const int f_lo = max(0, (s - kNfft / 2) / kHop + 1);
+  // Frames f with f*512 - 1024 <= s < f*512 + 1024, i.e. f in [q - 3, q] with
+  // q = floor((s + 1024) / 512) (s >= 0, so the division is a floor).
+  const int q = (s + kNfft / 2) / kHop;
+  const int f_hi = min(frames - 1, q);
+  const int f_lo = max(0, q - (kNfft / kHop - 1));
   float acc = 0.f, env = 0.f;
   const float* fb = frames_buf + static_cast<long long>(cc) * frames * kNfft;
   for (int f = f_lo; f <= f_hi; ++f) {

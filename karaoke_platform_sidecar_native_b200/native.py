@@ -66,6 +66,10 @@ _SIGNATURES = {
     "vocalarc_b200_stream": (_vp, [_vp]),
     "vocalarc_b200_take_device_error": (ctypes.c_int, [_vp]),
     "vocalarc_b200_set_precision": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "vocalarc_b200_launch_count": (ctypes.c_longlong, [_vp]),
+    "vocalarc_b200_trace_begin": (ctypes.c_int, [_vp]),
+    "vocalarc_b200_trace_mark": (ctypes.c_int, [_vp, ctypes.c_char_p]),
+    "vocalarc_b200_trace_end": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int]),
     "vocalarc_b200_stage_gemm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int,
                                                 ctypes.c_int, _vp, _vp]),
     "vocalarc_b200_stage_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -190,6 +194,25 @@ class Provider:
 
     def take_device_error(self) -> int:
         return self.lib.vocalarc_b200_take_device_error(self.handle)
+
+    @property
+    def launch_count(self) -> int:
+        return int(self.lib.vocalarc_b200_launch_count(self.handle))
+
+    def trace_begin(self):
+        self.check(self.lib.vocalarc_b200_trace_begin(self.handle), "trace_begin")
+
+    def trace_mark(self, what: str):
+        self.lib.vocalarc_b200_trace_mark(self.handle, what.encode())
+
+    def trace_end(self) -> dict:
+        buf = ctypes.create_string_buffer(1 << 16)
+        self.check(self.lib.vocalarc_b200_trace_end(self.handle, buf, len(buf)), "trace_end")
+        out = {}
+        for line in buf.value.decode().splitlines():
+            name, count, ms = line.split("\t")
+            out[name] = (int(count), float(ms))
+        return out
 
     # ---- stages (device pointers) --------------------------------------
     def stage_gemm(self, epilogue, a, b, m, n, k, bias, out):
