@@ -292,9 +292,10 @@ def main():
             dist.barrier()
 
     # ---- device-resident timed region
-    bus = torch.cuda.get_device_properties(local_rank).pci_bus_id if hasattr(
-        torch.cuda.get_device_properties(local_rank), "pci_bus_id") else ""
-    sampler = ClockSampler([bus] if bus else [])
+    props = torch.cuda.get_device_properties(local_rank)
+    bus = "%08X:%02X:%02X.0" % (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", 0),
+                                getattr(props, "pci_device_id", 0))
+    sampler = ClockSampler([bus])
     barrier()
     torch.cuda.synchronize()
     provider.synchronize()
