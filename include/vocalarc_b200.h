@@ -83,6 +83,21 @@ int vocalarc_b200_stage_stft(native_gpu *gpu, const float *audio, int segments, 
 /* iSTFT of spec*mask (both [segments][T][1025][2][2]) -> [segments][2][length]. */
 int vocalarc_b200_stage_istft(native_gpu *gpu, const float *spec, const float *mask, int segments,
                               int length, float *audio);
+/* Same result as vocalarc_b200_stage_istft, but allocates no device memory,
+   for callers that cannot call cudaMalloc while they process audio (a
+   real-time audio thread such as a plugin's process callback, where a call
+   that can block or synchronise the device is not allowed, or an application
+   whose GPU memory budget is fixed when it loads the library).  No
+   counterpart in the reference.  The frame scratch is a fixed 32 MiB device
+   array that every GPU which loads this library holds (from its first call on
+   that device at the latest) until the process exits; it serves at most segments * (length/512 + 1) <= 2048 frames (one
+   881,559-sample chunk), and larger requests are refused (return 0 with a
+   message on stderr).  The first call on a device looks up the array's device
+   address (cudaGetSymbolAddress) and should come before any stream capture.
+   All calls share that array and it keeps the last call's contents: calls
+   that can overlap on the GPU (other streams, other host threads) race. */
+int vocalarc_b200_stage_istft_noalloc(native_gpu *gpu, const float *spec, const float *mask, int segments,
+                                      int length, float *audio);
 /* Band split of spec (loaded model) -> x [segments][90][T][256] fp32. */
 int vocalarc_b200_stage_band_split(native_gpu *gpu, const float *spec, int segments, int frames, float *x);
 /* One transformer block (loaded model, layer, axis 0 = time / 1 = band) in

@@ -761,6 +761,19 @@ bool active(const native_gpu* g) { return g != nullptr && g->enabled; }
 
 }  // namespace
 
+namespace vab {
+// Read-only view of a provider for entry points defined in other translation
+// units: its device, stream and the window / twiddle tables made at creation.
+bool provider_view(native_gpu* g, int* device, cudaStream_t* stream, const float** window, const float2** twiddle) {
+  if (!active(g)) return false;
+  *device = g->device;
+  *stream = g->stream;
+  *window = g->d_window;
+  *twiddle = g->d_twiddle;
+  return true;
+}
+}  // namespace vab
+
 // ==================================================================== C ABI
 extern "C" {
 
