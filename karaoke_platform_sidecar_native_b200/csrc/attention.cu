@@ -203,12 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto accumulate_o = [&](int i, float alpha) -> bool {
       const int st = i % NBUF;
       const uint32_t par = static_cast<uint32_t>(i / NBUF) & 1u;
-      if (!mbar_wait(&o_full[st], par, abort_flag, args.err, kErrWaitSoftmax)) return false;
+      if (!mbar_wait_warp(&o_full[st], par, abort_flag, args.err, kErrWaitSoftmax)) return false;
       tc_fence_after();
       uint32_t r0[32], r1[32];
       tmem_ld32(tmem_o + st * kDimHead + lane_off, r0);
       tmem_ld32(tmem_o + st * kDimHead + 32 + lane_off, r1);
       tmem_wait_ld();
+      reg_fence(r0);
+      reg_fence(r1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_empty[st]);
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < nkv; ++j) {
       const int st = j % NBUF;
       const uint32_t par = static_cast<uint32_t>(j / NBUF) & 1u;
-      if (!mbar_wait(&s_full[st], par, abort_flag, args.err, kErrWaitSoftmax)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[st], par, abort_flag, args.err, kErrWaitSoftmax)) { ok = false; break; }
       tc_fence_after();
       const int kv0 = j * kTile;
       const int valid = length - kv0;
@@ -237,12 +239,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[32];
           tmem_ld32(s_addr + c, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
         } else {
           uint32_t r[16];
           tmem_ld16(s_addr + c, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int q = 0; q < 16; ++q) v[q] = __uint_as_float(r[q]);
 #pragma unroll
@@ -264,12 +268,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[32];
           tmem_ld32(s_addr + c, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
         } else {
           uint32_t r[16];
           tmem_ld16(s_addr + c, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int q = 0; q < 16; ++q) v[q] = __uint_as_float(r[q]);
 #pragma unroll
@@ -355,16 +361,349 @@ cudaError_t launch_typed(const CUtensorMap& map, const AttnArgs& args, cudaStrea
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Long sequences (L > 128): one CTA computes two 128-query tiles (A, B) of one
+// (sequence, head) that share every K/V tile.  Warps 2-5 own tile A, warps 6-9
+// tile B (one query row per thread).  O accumulates in TMEM across KV tiles;
+// a row's reference maximum m is raised only when a tile's maximum exceeds it
+// by more than 2^8 in exp2 units, in which case that row of O (TMEM) and its
+// running sum are rescaled -- otherwise P = exp2((s - m) c) <= 256 stays exact
+// enough in 16 bits and no O traffic is needed.
+constexpr int kPairThreads = 320;
+constexpr float kRescaleLog2 = 8.0f;
+
+struct PairSmem {
+  static constexpr int kQ = 0;                       // 2 x 16 KB
+  static constexpr int kK = kQ + 2 * kQBytes;        // 2 stages x 16 KB
+  static constexpr int kV = kK + 2 * kQBytes;        // 2 stages x 16 KB
+  static constexpr int kP = kV + 2 * kQBytes;        // 2 tiles x 32 KB
+  static constexpr int kBar = kP + 2 * kPBytes;
+  static constexpr int kBytes = 1024 + kBar + 256;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    attention_pair_kernel(const __grid_constant__ CUtensorMap map, const AttnArgs args) {
+  using L = PairSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::kQ;
+  uint8_t* sK = smem + L::kK;
+  uint8_t* sV = smem + L::kV;
+  uint8_t* sP = smem + L::kP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;     // [tile]
+  uint64_t* s_empty = bars + 7;    // [tile]
+  uint64_t* p_full = bars + 9;     // [tile]
+  uint64_t* o_full = bars + 11;    // [tile]
+  uint64_t* drain = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const long long bid = blockIdx.x;
+  const int q_pairs = (args.q_tiles + 1) / 2;
+  const int pair = static_cast<int>(bid % q_pairs);
+  const long long rest = bid / q_pairs;
+  const int head = static_cast<int>(rest % kHeads);
+  const long long seq = rest / kHeads;
+  const int q0 = pair * 2 * kTile;
+  const int length = args.length;
+  const int ntiles = (q0 + kTile < length) ? 2 : 1;
+  const int nkv = (length + kTile - 1) / kTile;
+  int c_a, c_b;
+  if (args.pos_dim == 1) {
+    c_a = static_cast<int>(seq % args.d2);
+    c_b = static_cast<int>(seq / args.d2);
+  } else {
+    c_a = static_cast<int>(seq % args.d1);
+    c_b = static_cast<int>(seq / args.d1);
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384).
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch(&map);
+      auto load_tile = [&](uint8_t* dst, uint64_t* bar, int col, int pos) {
+        if (args.pos_dim == 1)
+          tma_load_4d(dst, &map, bar, col, pos, c_a, c_b);
+        else
+          tma_load_4d(dst, &map, bar, col, c_a, pos, c_b);
+      };
+      mbar_arrive_expect_tx(q_full, ntiles * kQBytes);
+      load_tile(sQ, q_full, head * kDimHead, q0);
+      if (ntiles == 2) load_tile(sQ + kQBytes, q_full, head * kDimHead, q0 + kTile);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        const uint32_t par = static_cast<uint32_t>(j >> 1) & 1u;
+        if (!mbar_wait(&kv_empty[st], par ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kQBytes);
+        load_tile(sK + st * kQBytes, &kv_full[st], kDimInner + head * kDimHead, j * kTile);
+        load_tile(sV + st * kQBytes, &kv_full[st], 2 * kDimInner + head * kDimHead, j * kTile);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t bf = ElemTraits<T>::kBf16;
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i & 1;
+        const int nc = min(kTile, round16(length - i * kTile));
+        const uint32_t idesc = idesc_f16(kTile, kDimHead, bf, 0, 1);
+        const uint32_t v_addr = smem_u32(sV + st * kQBytes);
+        for (int x = 0; x < ntiles; ++x) {
+          if (!mbar_wait(&p_full[x], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitMma)) return false;
+          tc_fence_after();
+          const uint32_t p_addr = smem_u32(sP + x * kPBytes);
+          for (int kk = 0; kk < nc / 16; ++kk) {
+            const uint64_t da = sw128_desc(p_addr + (kk >> 2) * (kTile * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t db = sw128_desc(v_addr + kk * 2048, 8192, 1024);
+            umma_f16(tmem_base + 256 + x * kDimHead, da, db, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&o_full[x]);
+        }
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, args.err, kErrWaitMma);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, args.err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        const int nc = min(kTile, round16(length - j * kTile));
+        const uint32_t idesc = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
+        const uint32_t k_addr = smem_u32(sK + st * kQBytes);
+        for (int x = 0; x < ntiles && ok; ++x) {
+          if (!mbar_wait(&s_empty[x], (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag, args.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sQ + x * kQBytes);
+#pragma unroll
+          for (int kk = 0; kk < kDimHead / 16; ++kk) {
+            const uint64_t da = sw128_desc(q_addr + kk * 32, 16, 1024);
+            const uint64_t db = sw128_desc(k_addr + kk * 32, 16, 1024);
+            umma_f16(tmem_base + x * kTile, da, db, idesc, kk != 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[x]);
+        }
+        if (ok && j > 0 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok) issue_pv(nkv - 1);
+      umma_commit(drain);
+      wait_drain(drain, 0, args.err);
+    }
+    __syncwarp();
+  } else {
+    const int x = (warp - 2) >> 2;          // query tile of this warp
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_addr = tmem_base + x * kTile + lane_off;
+    const uint32_t o_addr = tmem_base + 256 + x * kDimHead + lane_off;
+    uint8_t* p_base = sP + x * kPBytes + (row >> 3) * 1024 + (row & 7) * 128;
+    bool ok = x < ntiles;
+    float m_ref = -INFINITY;   // reference maximum (raw score units)
+    float l_run = 0.f;
+    for (int j = 0; ok && j < nkv; ++j) {
+      if (!mbar_wait_warp(&s_full[x], static_cast<uint32_t>(j) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int valid = length - j * kTile;
+      const int nc = min(kTile, round16(valid));
+      // All 128 S columns are read; columns >= valid (stale or never written
+      // by a narrower MMA) are masked below.
+      uint32_t ra[32], rb[32], rc[32], rd[32];
+      tmem_ld32(s_addr + 0, ra);
+      tmem_ld32(s_addr + 32, rb);
+      tmem_ld32(s_addr + 64, rc);
+      tmem_ld32(s_addr + 96, rd);
+      tmem_wait_ld();
+      reg_fence(ra);
+      reg_fence(rb);
+      reg_fence(rc);
+      reg_fence(rd);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[x]);
+      float v[kTile];
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        v[q] = __uint_as_float(ra[q]);
+        v[32 + q] = __uint_as_float(rb[q]);
+        v[64 + q] = __uint_as_float(rc[q]);
+        v[96 + q] = __uint_as_float(rd[q]);
+      }
+      if (valid < kTile) {   // only the last KV tile has keys past the end
+#pragma unroll
+        for (int q = 0; q < kTile; ++q)
+          if (q >= valid) v[q] = -INFINITY;
+      }
+      // Row maximum as a tree over 8 independent accumulators.
+      float mxs[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mxs[a] = v[a];
+#pragma unroll
+      for (int q = 8; q < kTile; ++q) mxs[q & 7] = fmaxf(mxs[q & 7], v[q]);
+      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+      // Raise the reference maximum only when this tile would exceed 2^8.
+      const bool raise = (mx - m_ref) * kScaleLog2 > kRescaleLog2;
+      const float m_new = raise ? mx : m_ref;
+      const float factor = raise ? ex2_approx((m_ref - m_new) * kScaleLog2) : 1.0f;   // 0 when m_ref = -inf
+      const float mscaled = m_new * kScaleLog2;
+      float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[kTile / 2];   // P packed to 16-bit pairs, freeing the fp32 scores
+#pragma unroll
+      for (int q = 0; q < kTile; q += 2) {
+        const float p0 = ex2_approx(fmaf(v[q], kScaleLog2, -mscaled));
+        const float p1 = ex2_approx(fmaf(v[q + 1], kScaleLog2, -mscaled));
+        sums[(q >> 1) & 7] += p0 + p1;
+        pk[q / 2] = ElemTraits<T>::pack2(p0, p1);
+      }
+      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+      if (j > 0) {
+        // PV of the previous tile must be complete before P is overwritten and
+        // before this row of O is rescaled.
+        if (!mbar_wait_warp(&o_full[x], static_cast<uint32_t>(j - 1) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, raise)) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t r[32];
+            tmem_ld32(o_addr + half * 32, r);
+            tmem_wait_ld();
+            reg_fence(r);
+#pragma unroll
+            for (int d = 0; d < 32; ++d) r[d] = __float_as_uint(__uint_as_float(r[d]) * factor);
+            tmem_st32(o_addr + half * 32, r);
+          }
+          tmem_wait_st();
+        }
+      }
+      l_run = l_run * factor + sum;
+      m_ref = m_new;
+#pragma unroll
+      for (int g = 0; g < kTile / 8; ++g) {
+        if (g * 8 < nc) {
+          const int atom = g >> 3;
+          const int chunk16 = g & 7;
+          *reinterpret_cast<uint4*>(p_base + atom * (kTile * 128) + ((chunk16 ^ (row & 7)) << 4)) =
+              make_uint4(pk[g * 4 + 0], pk[g * 4 + 1], pk[g * 4 + 2], pk[g * 4 + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[x]);
+    }
+    if (ok && mbar_wait_warp(&o_full[x], static_cast<uint32_t>(nkv - 1) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      tmem_ld32(o_addr, r0);
+      tmem_ld32(o_addr + 32, r1);
+      tmem_wait_ld();
+      reg_fence(r0);
+      reg_fence(r1);
+      const int qpos = q0 + x * kTile + row;
+      if (qpos < length) {
+        long long R;
+        if (args.pos_dim == 1)
+          R = seq * args.d1 + qpos;
+        else
+          R = (static_cast<long long>(c_b) * args.d2 + qpos) * args.d1 + c_a;
+        const float scale = __ldg(args.gates + R * kHeads + head) / l_run;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(args.out) + R * kDimInner + head * kDimHead);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 w;
+          w.x = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 0]) * scale, __uint_as_float(r0[g * 8 + 1]) * scale);
+          w.y = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 2]) * scale, __uint_as_float(r0[g * 8 + 3]) * scale);
+          w.z = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 4]) * scale, __uint_as_float(r0[g * 8 + 5]) * scale);
+          w.w = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 6]) * scale, __uint_as_float(r0[g * 8 + 7]) * scale);
+          dst[g] = w;
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 w;
+          w.x = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 0]) * scale, __uint_as_float(r1[g * 8 + 1]) * scale);
+          w.y = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 2]) * scale, __uint_as_float(r1[g * 8 + 3]) * scale);
+          w.z = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 4]) * scale, __uint_as_float(r1[g * 8 + 5]) * scale);
+          w.w = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 6]) * scale, __uint_as_float(r1[g * 8 + 7]) * scale);
+          dst[4 + g] = w;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+template <typename T>
+cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attention_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         PairSmem::kBytes);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const long long blocks = static_cast<long long>((args.q_tiles + 1) / 2) * kHeads * args.sequences;
+  if (blocks <= 0) return cudaSuccess;
+  if (blocks > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
+  attention_pair_kernel<T><<<static_cast<unsigned>(blocks), kPairThreads, PairSmem::kBytes, stream>>>(map, args);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_attention(bool bf16, const CUtensorMap& map_qkv, const AttnArgs& args, cudaStream_t stream) {
   // Single-tile sequences (band axis, L <= 128) use one buffer of each kind:
-  // 80 KB of shared memory and 256 TMEM columns, two CTAs per SM.
+  // 80 KB of shared memory and 256 TMEM columns, two CTAs per SM.  Longer
+  // sequences use the two-query-tile kernel.
   const bool single = args.length <= kTile;
   if (bf16)
-    return single ? launch_typed<__nv_bfloat16, 1>(map_qkv, args, stream)
-                  : launch_typed<__nv_bfloat16, 2>(map_qkv, args, stream);
-  return single ? launch_typed<__half, 1>(map_qkv, args, stream) : launch_typed<__half, 2>(map_qkv, args, stream);
+    return single ? launch_typed<__nv_bfloat16, 1>(map_qkv, args, stream) : launch_pair<__nv_bfloat16>(map_qkv, args, stream);
+  return single ? launch_typed<__half, 1>(map_qkv, args, stream) : launch_pair<__half>(map_qkv, args, stream);
 }
 
 }  // namespace vab

@@ -3,8 +3,9 @@
 // One CTA per SM walks a static tile schedule.  Warp 0 issues TMA loads of
 // 128x64 A and (n_size)x64 B tiles into a 4-stage 128-byte-swizzled ring, warp
 // 1 (one thread) issues tcgen05.mma (M=128, N=n_size<=256, K=16) into one of
-// two TMEM accumulators, and warps 2-5 drain the other accumulator with
-// tcgen05.ld and apply a fused epilogue (RoPE, bias+GELU, fp32 residual, tanh,
+// two TMEM accumulators, and warps 2-9 (two per TMEM lane quarter, splitting
+// the columns) drain the other accumulator with tcgen05.ld and apply a fused
+// epilogue (RoPE, bias+GELU, fp32 residual, tanh,
 // GLU + complex-mask scatter).  The reference computes these products with
 // cuBLAS SGEMM plus separate SIMT kernels (native/native_gpu_cuda.cu:540-552,
 // :279-297, :414-426, :453-485).
@@ -23,7 +24,8 @@ constexpr int kBK = 64;
 constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;          // TMA warp, MMA warp, 8 epilogue warps
+constexpr int kEpiWarps = 8;
 constexpr int kTmemCols = 512;           // two 128x256 fp32 accumulators
 constexpr size_t kSmemBytes = 1024 + kStages * (kABytes + kBBytes) + 256;
 
@@ -82,7 +84,7 @@ __device__ __forceinline__ void store_row16(T* dst, const float* v, int count) {
 // of tile row `r` (global A row R).
 template <typename T, int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const TileInfo& ti, long long R, int c,
-                                               float (&v)[32], int count) {
+                                               float (&v)[32], int count, const float4 (&rope)[8]) {
   const int n = ti.n0 + c;  // output column of v[0]
   if (EPI == kEpiStore || EPI == kEpiGelu || EPI == kEpiTanhBand) {
     const float* bias = args.bias;
@@ -108,17 +110,19 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const TileI
     for (int q = 0; q < 8; ++q)
       if (q * 4 < count) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   } else if (EPI == kEpiQkvRope) {
+    // rope[i] = (cos, sin, cos, sin) of pairs 2i, 2i+1 of this 32-column chunk
+    // (the chunk starts at column n, pair (n % 64) / 2, of a 64-wide head).
     if (n < args.rope_cols) {
-      const int pos = static_cast<int>((R / args.pos_div) % args.pos_mod);
-      const float2* table = args.rope + static_cast<long long>(pos) * (kDimHead / 2);
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        if (j < count) {
-          const float2 cs = __ldg(table + (((n + j) & (kDimHead - 1)) >> 1));
-          const float a = v[j], b = v[j + 1];
-          v[j] = a * cs.x - b * cs.y;
-          v[j + 1] = a * cs.y + b * cs.x;
-        }
+      for (int i = 0; i < 8; ++i) {
+        const float4 cs = rope[i];
+        float a = v[4 * i], b = v[4 * i + 1];
+        v[4 * i] = a * cs.x - b * cs.y;
+        v[4 * i + 1] = a * cs.y + b * cs.x;
+        a = v[4 * i + 2];
+        b = v[4 * i + 3];
+        v[4 * i + 2] = a * cs.z - b * cs.w;
+        v[4 * i + 3] = a * cs.w + b * cs.z;
       }
     }
     T* dst = static_cast<T*>(args.out) + R * args.ldo + n;
@@ -223,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -317,26 +321,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue warps 2..5
+    // ---------------- epilogue warps 2..9: lane quarter warp%4, column half
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     int it = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, args.err, kErrWaitEpilogue)) break;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, args.err, kErrWaitEpilogue)) break;
       tc_fence_after();
       const TileInfo ti = decode_tile(args, tile);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
       const long long R = static_cast<long long>(ti.a_row) + row;
       const bool valid = row < ti.m_valid;
-      for (int c = 0; c < ti.n_size; c += 32) {
+      // A 32-column chunk of this half always starts at column 32*half of a
+      // 64-wide head, so it uses RoPE pairs [16*half, 16*half + 16) of the
+      // row's position: load them once per tile.
+      float4 rope[8];
+      if (EPI == kEpiQkvRope) {
+        const int pos = static_cast<int>((R / args.pos_div) % args.pos_mod);
+        const float4* table = reinterpret_cast<const float4*>(args.rope + static_cast<long long>(pos) * (kDimHead / 2) + 16 * half);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rope[i] = valid && ti.n0 < args.rope_cols ? __ldg(table + i) : make_float4(1.f, 0.f, 1.f, 0.f);
+      }
+      for (int c = half * 32; c < ti.n_size; c += 64) {
         float v[32];
         int count;
         if (ti.n_size - c >= 32) {
           uint32_t r[32];
           tmem_ld32(taddr + c, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
           count = 32;
@@ -344,13 +360,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[16];
           tmem_ld16(taddr + c, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 #pragma unroll
           for (int j = 16; j < 32; ++j) v[j] = 0.f;
           count = 16;
         }
-        if (valid) epilogue_chunk<T, EPI>(args, ti, R, c, v, count);
+        if (valid) epilogue_chunk<T, EPI>(args, ti, R, c, v, count, rope);
       }
       tc_fence_before();
       __syncwarp();

@@ -476,8 +476,8 @@ bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan&
                 "norm+gates"))
     return false;
   CUtensorMap a;
-  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
   GemmArgs args = uniform_args(g, tokens, kQkvDim, kDim);
+  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
   args.out = g->qkv;
   args.ldo = kQkvDim;
   args.rope = g->d_rope;

@@ -44,6 +44,9 @@ struct GemmArgs {
   int tiles_per_chunk;  // grouped: entries of the table
   int chunk_rows;       // grouped: A-row offset between chunk replicas
   int b_box16;          // 1: B loaded as n_size/16 boxes of 16 rows
+  int a_strided;        // 1: A is a 3-D map (K, a_d1, a_d2) and a tile is 128 rows
+                        //    (g0 + r) * a_d1 + t at one t (uniform mode only)
+  int a_d1, a_d2;
   void* out;
   long long ldo;
   const float* bias;
@@ -66,6 +69,7 @@ inline int4 make_tile(int a_row, int b_row, int n0, int m_valid, int n_size, int
 bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t outer,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128,
                   bool bf16);
+bool make_tmap_3d_rows(CUtensorMap* map, const void* base, uint64_t k, uint64_t d1, uint64_t d2, bool bf16);
 bool make_tmap_4d(CUtensorMap* map, const void* base, int elem_bytes, const uint64_t dims[4],
                   const uint64_t strides_bytes[3], const uint32_t box[4], bool bf16);
 
