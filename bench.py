@@ -71,8 +71,9 @@ def kernel_work(name, chunks_per_launch):
     c, t = chunks_per_launch, FRAMES
     tokens = c * 90 * t
     flops = {
-        "qkv gemm": 2 * tokens * 256 * 1536,
+        "qkv gemm": 2 * tokens * 256 * (1536 + 8),
         "out gemm": 2 * tokens * 512 * 256,
+
         "ff1 gemm": 2 * tokens * 256 * 1024,
         "ff2 gemm": 2 * tokens * 1024 * 256,
         "attention (L>128)": 4 * 64 * 8 * (c * 90) * t * t,
@@ -81,9 +82,7 @@ def kernel_work(name, chunks_per_launch):
         "mask gemm 2": 2 * c * t * 2 * BAND_DIMS_SUM * 1024,
     }
     bytes_ = {
-        "norm+gates": tokens * (256 * 4 + 256 * 2 + 8 * 4),
-        "ff norm": tokens * (256 * 4 + 256 * 2),
-        "final norm": tokens * (256 * 4 + 256 * 2),
+        "row stats": tokens * (256 * 4 + 256 * 2 + 4),
         "stft": c * (2 * CHUNK * 4 + t * 1025 * 16),
         "band split": c * t * (1025 * 16 + 90 * 256 * 4),
         "istft": c * t * (2 * 1025 * 16 + 2 * 2048 * 4),

@@ -1,14 +1,26 @@
 // Persistent tcgen05 GEMM for sm_100a:  C[M][N] = A[M][K] * B[N][K]^T.
 //
 // One CTA per SM walks a static tile schedule.  Warp 0 issues TMA loads of
-// 128x64 A and (n_size)x64 B tiles into a 4-stage 128-byte-swizzled ring, warp
+// 128x64 A and (n_size)x64 B tiles into a 3-stage 128-byte-swizzled ring, warp
 // 1 (one thread) issues tcgen05.mma (M=128, N=n_size<=256, K=16) into one of
-// two TMEM accumulators, and warps 2-9 (two per TMEM lane quarter, splitting
-// the columns) drain the other accumulator with tcgen05.ld and apply a fused
-// epilogue (RoPE, bias+GELU, fp32 residual, tanh,
-// GLU + complex-mask scatter).  The reference computes these products with
-// cuBLAS SGEMM plus separate SIMT kernels (native/native_gpu_cuda.cu:540-552,
-// :279-297, :414-426, :453-485).
+// two TMEM accumulators, and warps 2-9 (two per TMEM lane quarter, each owning
+// 128 columns) drain the other accumulator with tcgen05.ld.
+//
+// Epilogue I/O is staged: each epilogue warp writes its 32-row block into a
+// swizzled shared-memory buffer and a TMA tensor store moves it to global
+// memory (and the fp32 residual comes in by TMA load the same way), so global
+// traffic is whole lines instead of one row per thread.
+//
+// RMSNorm is folded: the gamma of the norm that precedes a GEMM is multiplied
+// into that GEMM's weights at load time, the producer of x writes a 16-bit copy
+// of x and the per-row factor inv = sqrt(256) / sqrt(sum x^2 + 1e-12), and the
+// consumer scales its accumulator row by inv:  (x * inv * gamma) W^T =
+// inv * (x (gamma o W)^T).  The head gates (Linear 256 -> 8 of the normed row)
+// are the 16-column tail tile of the QKV GEMM.
+//
+// The reference computes these products with cuBLAS SGEMM plus separate SIMT
+// kernels (native/native_gpu_cuda.cu:540-552, :258-297, :403-426, :453-485);
+// the CPU semantics are transformer_forward (native/vocalarc_separation.c:836-873).
 #include <cstdio>
 
 #include "ptx.cuh"
@@ -21,13 +33,17 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kThreads = 320;          // TMA warp, MMA warp, 8 epilogue warps
+constexpr int kThreads = 320;            // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kEpiWarps = 8;
 constexpr int kTmemCols = 512;           // two 128x256 fp32 accumulators
-constexpr size_t kSmemBytes = 1024 + kStages * (kABytes + kBBytes) + 256;
+constexpr int kStageBuf = 4096;          // one epilogue staging buffer: 32 rows x 128 B
+constexpr int kRedBytes = 2 * 2 * 128 * 4;
+constexpr int kBarBytes = 512;
+constexpr int kSmemBytes =
+    1024 + kStages * (kABytes + kBBytes) + kEpiWarps * 2 * kStageBuf + kRedBytes + kBarBytes;
 
 __constant__ int c_band_first[kBands];
 __constant__ int c_band_dim[kBands];
@@ -39,13 +55,14 @@ struct TileInfo {
 __device__ __forceinline__ TileInfo decode_tile(const GemmArgs& args, int tile) {
   TileInfo t;
   if (args.tiles == nullptr) {
-    const int m_blk = tile / args.n_tiles;
-    const int n_blk = tile - m_blk * args.n_tiles;
+    const int per_m = args.n_tiles + (args.gate_tile ? 1 : 0);
+    const int m_blk = tile / per_m;
+    const int n_blk = tile - m_blk * per_m;
     t.a_row = m_blk * kBM;
     t.m_valid = min(kBM, args.m_rows - t.a_row);
     t.b_row = n_blk * kBN;
     t.n0 = n_blk * kBN;
-    t.n_size = kBN;
+    t.n_size = n_blk < args.n_tiles ? kBN : 16;   // the gate tile: 8 gate rows + 8 zero rows
     t.band = 0;
   } else {
     const int chunk = tile / args.tiles_per_chunk;
@@ -64,9 +81,25 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 
 __device__ __forceinline__ float sigmoidf(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk q of row r in a 128-byte-row, 128B-swizzled buffer.
+__device__ __forceinline__ int sw128(int r, int q) { return r * 128 + ((q ^ (r & 7)) << 4); }
+// Same for 64-byte rows and the 64B swizzle.
+__device__ __forceinline__ int sw64(int r, int q) { return r * 64 + ((q ^ ((r >> 1) & 3)) << 4); }
+
 template <typename T>
 __device__ __forceinline__ void store_row16(T* dst, const float* v, int count) {
-  // count is 16 or 32; dst is 32-byte aligned.
+  // Direct per-row store (grouped mask and test epilogues). count is 16 or 32.
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -80,109 +113,284 @@ __device__ __forceinline__ void store_row16(T* dst, const float* v, int count) {
   }
 }
 
-// Applies the epilogue to `count` (16 or 32) accumulator columns [c, c+count)
-// of tile row `r` (global A row R).
+// Per-warp epilogue state: two staging buffers, their TMA-load barriers and phases.
+struct EpiWarp {
+  uint8_t* buf[2];
+  uint64_t* bar[2];
+  uint32_t phase[2];
+  int cur;
+  int lane;
+};
+
+// ---------------------------------------------------------------- 16-bit outputs
+// QKV (+RoPE, row scale), FF1 (+bias, GELU, row scale), plain store.  This warp
+// owns columns [128*half, 128*half + 128) of the tile in two 64-column steps.
 template <typename T, int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const TileInfo& ti, long long R, int c,
-                                               float (&v)[32], int count, const float4 (&rope)[8]) {
-  const int n = ti.n0 + c;  // output column of v[0]
-  if (EPI == kEpiStore || EPI == kEpiGelu || EPI == kEpiTanhBand) {
-    const float* bias = args.bias;
-    const int bias_base = (EPI == kEpiTanhBand) ? (ti.b_row + c) : n;
-    if (bias != nullptr) {
+__device__ __forceinline__ void epilogue_out16(const GemmArgs& args, const CUtensorMap* map_out, const TileInfo& ti,
+                                               EpiWarp& ew, uint32_t taddr, int half, int row, long long R, bool valid,
+                                               int row0) {
+  const float inv = (args.row_inv != nullptr && valid) ? __ldg(args.row_inv + R) : 1.0f;
+  float4 rope[16];
+  const bool do_rope = EPI == kEpiQkvRope && ti.n0 < args.rope_cols;
+  if (EPI == kEpiQkvRope) {
+    const int pos = static_cast<int>((R / args.pos_div) % args.pos_mod);
+    const float4* table = reinterpret_cast<const float4*>(args.rope + static_cast<long long>(pos) * (kDimHead / 2));
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < count) v[j] += __ldg(bias + bias_base + j);
-    }
-    if (EPI == kEpiGelu) {
+    for (int i = 0; i < 16; ++i) rope[i] = (valid && do_rope) ? __ldg(table + i) : make_float4(1.f, 0.f, 1.f, 0.f);
+  }
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-    }
-    if (EPI == kEpiTanhBand) {
+  for (int s = 0; s < 2; ++s) {
+    const int c = half * 128 + s * 64;   // tile column of this step
+    uint8_t* buf = ew.buf[ew.cur];
+    if (ew.lane == 0) bulk_wait_read1();   // the store that last used this buffer has read it
+    __syncwarp();
+    const int n = ti.n0 + c;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
-    }
-    T* dst = static_cast<T*>(args.out) + R * args.ldo + n;
-    store_row16<T>(dst, v, count);
-  } else if (EPI == kEpiStoreF32) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(args.out) + R * args.ldo + n);
+    for (int hh = 0; hh < 2; ++hh) {   // two 32-column halves of the 64-column step
+      uint32_t r[32];
+      tmem_ld32(taddr + c + 32 * hh, r);
+      tmem_wait_ld();
+      reg_fence(r);
+      float v[32];
 #pragma unroll
-    for (int q = 0; q < 8; ++q)
-      if (q * 4 < count) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-  } else if (EPI == kEpiQkvRope) {
-    // rope[i] = (cos, sin, cos, sin) of pairs 2i, 2i+1 of this 32-column chunk
-    // (the chunk starts at column n, pair (n % 64) / 2, of a 64-wide head).
-    if (n < args.rope_cols) {
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * inv;
+      if (EPI == kEpiGelu || (EPI == kEpiStore && args.bias != nullptr)) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 cs = rope[i];
-        float a = v[4 * i], b = v[4 * i + 1];
-        v[4 * i] = a * cs.x - b * cs.y;
-        v[4 * i + 1] = a * cs.y + b * cs.x;
-        a = v[4 * i + 2];
-        b = v[4 * i + 3];
-        v[4 * i + 2] = a * cs.z - b * cs.w;
-        v[4 * i + 3] = a * cs.w + b * cs.z;
+        for (int q = 0; q < 8; ++q) {
+          const float4 b = __ldg(reinterpret_cast<const float4*>(args.bias + n + 32 * hh) + q);
+          v[4 * q] += b.x;
+          v[4 * q + 1] += b.y;
+          v[4 * q + 2] += b.z;
+          v[4 * q + 3] += b.w;
+        }
+      }
+      if (EPI == kEpiGelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+      }
+      if (do_rope) {
+        // A 64-column step is one head: pairs (2i, 2i+1) rotate by rope pair i.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 cs = rope[8 * hh + i];
+          float a = v[4 * i], b = v[4 * i + 1];
+          v[4 * i] = a * cs.x - b * cs.y;
+          v[4 * i + 1] = a * cs.y + b * cs.x;
+          a = v[4 * i + 2];
+          b = v[4 * i + 3];
+          v[4 * i + 2] = a * cs.z - b * cs.w;
+          v[4 * i + 3] = a * cs.w + b * cs.z;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = ElemTraits<T>::pack2(v[q * 8 + 0], v[q * 8 + 1]);
+        w.y = ElemTraits<T>::pack2(v[q * 8 + 2], v[q * 8 + 3]);
+        w.z = ElemTraits<T>::pack2(v[q * 8 + 4], v[q * 8 + 5]);
+        w.w = ElemTraits<T>::pack2(v[q * 8 + 6], v[q * 8 + 7]);
+        *reinterpret_cast<uint4*>(buf + sw128(row & 31, 4 * hh + q)) = w;
       }
     }
-    T* dst = static_cast<T*>(args.out) + R * args.ldo + n;
-    store_row16<T>(dst, v, count);
-  } else if (EPI == kEpiResidual) {
-    float4* dst = reinterpret_cast<float4*>(args.resid + R * args.ldr + n);
-    const float* bias = args.bias;
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (ew.lane == 0) {
+      tma_store_2d(map_out, buf, n, row0);
+      bulk_commit();
+    }
+    ew.cur ^= 1;
+  }
+}
+
+// ---------------------------------------------------------------- fp32 residual + row statistics
+// resid += acc (+ bias); writes resid (fp32), its 16-bit copy and, combined with
+// the other column half through shared memory, inv = sqrt(256)/sqrt(sum + 1e-12)
+// for the row (transformer_forward's residual_add + the following rms_norm's
+// scale, vocalarc_separation.c:864-866, :849, rms_norm_row_scalar :419-424).
+template <typename T>
+__device__ __forceinline__ void epilogue_residual(const GemmArgs& args, const CUtensorMap* map_res,
+                                                  const CUtensorMap* map_x16, const TileInfo& ti, EpiWarp& ew,
+                                                  uint32_t taddr, int half, int quarter, int row, long long R,
+                                                  bool valid, int row0, int parity, float* red) {
+  float ss = 0.f;
+  // Prefetch the first residual block of this warp's columns.
+  if (ew.lane == 0) {
+    bulk_wait_read0();
+    mbar_arrive_expect_tx(ew.bar[ew.cur], kStageBuf);
+    tma_load_2d(ew.buf[ew.cur], map_res, ew.bar[ew.cur], ti.n0 + half * 128, row0);
+  }
+  __syncwarp();
+#pragma unroll 1
+  for (int s = 0; s < 4; ++s) {
+    const int b = ew.cur;
+    const int c = half * 128 + s * 32;
+    const int n = ti.n0 + c;
+    if (ew.lane == 0 && s + 1 < 4) {
+      bulk_wait_read0();   // both stores from the other buffer have read it
+      mbar_arrive_expect_tx(ew.bar[b ^ 1], kStageBuf);
+      tma_load_2d(ew.buf[b ^ 1], map_res, ew.bar[b ^ 1], n + 32, row0);
+    }
+    __syncwarp();
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);
+    tmem_wait_ld();
+    reg_fence(r);
+    // Bounded wait for the residual block (TMA load issued above).
+    {
+      const unsigned long long start = global_timer_ns();
+      while (!mbar_try_wait(ew.bar[b], ew.phase[b])) {
+        if (global_timer_ns() - start > kWaitLimitNs) {
+          atomicCAS(args.err, 0, kErrWaitEpilogue);
+          break;
+        }
+      }
+    }
+    ew.phase[b] ^= 1u;
+    uint8_t* buf = ew.buf[b];
+    float x[32];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      if (q * 4 < count) {
-        float4 x = dst[q];
-        float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-        if (bias != nullptr) {
-          b0 = __ldg(bias + n + 4 * q);
-          b1 = __ldg(bias + n + 4 * q + 1);
-          b2 = __ldg(bias + n + 4 * q + 2);
-          b3 = __ldg(bias + n + 4 * q + 3);
-        }
-        x.x += v[4 * q] + b0;
-        x.y += v[4 * q + 1] + b1;
-        x.z += v[4 * q + 2] + b2;
-        x.w += v[4 * q + 3] + b3;
-        dst[q] = x;
-      }
+      float4 xv = *reinterpret_cast<const float4*>(buf + sw128(row & 31, q));
+      float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (args.bias != nullptr) bv = __ldg(reinterpret_cast<const float4*>(args.bias + n) + q);
+      xv.x += __uint_as_float(r[4 * q]) + bv.x;
+      xv.y += __uint_as_float(r[4 * q + 1]) + bv.y;
+      xv.z += __uint_as_float(r[4 * q + 2]) + bv.z;
+      xv.w += __uint_as_float(r[4 * q + 3]) + bv.w;
+      x[4 * q] = xv.x;
+      x[4 * q + 1] = xv.y;
+      x[4 * q + 2] = xv.z;
+      x[4 * q + 3] = xv.w;
+      *reinterpret_cast<float4*>(buf + sw128(row & 31, q)) = xv;
     }
-  } else if (EPI == kEpiGluMask) {
-    // Columns hold interleaved (value, gate) pairs of band `ti.band`; pair p
-    // is mask component p of the band: frequency first + p/4, channel
-    // (p/2)%2, re/im p%2 (mask_band, vocalarc_separation.c:1330-1338).
-    const int band = ti.band;
-    const int dim = c_band_dim[band];
-    const int first = c_band_first[band];
-    const long long seq = R / args.frames;
-    const int t = static_cast<int>(R - seq * args.frames);
-    const long long chunk = seq / kBands;
-    const float* bias = args.bias + ti.b_row + c;
-    const int p0 = n >> 1;
-    if (args.mask_ref_layout) {
+    if (valid) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int p = p0 + j;
-        if (2 * j < count && p < dim) {
-          const float value = v[2 * j] + __ldg(bias + 2 * j);
-          const float gate = v[2 * j + 1] + __ldg(bias + 2 * j + 1);
-          const int f = first + (p >> 2), ch = (p >> 1) & 1, ri = p & 1;
-          float* dst = static_cast<float*>(args.out) +
-                       ((static_cast<long long>(f) * kChannels + ch) * args.frames + t) * 2 + ri;
-          *dst = value * sigmoidf(gate);
-        }
-      }
+      for (int j = 0; j < 32; ++j) ss += x[j] * x[j];
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (ew.lane == 0) {
+      tma_store_2d(map_res, buf, n, row0);
+      bulk_commit();
+      bulk_wait_read0();   // the fp32 block is read out; reuse the buffer for the 16-bit copy
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = ElemTraits<T>::pack2(x[q * 8 + 0], x[q * 8 + 1]);
+      w.y = ElemTraits<T>::pack2(x[q * 8 + 2], x[q * 8 + 3]);
+      w.z = ElemTraits<T>::pack2(x[q * 8 + 4], x[q * 8 + 5]);
+      w.w = ElemTraits<T>::pack2(x[q * 8 + 6], x[q * 8 + 7]);
+      *reinterpret_cast<uint4*>(buf + sw64(row & 31, q)) = w;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (ew.lane == 0) {
+      tma_store_2d(map_x16, buf, n, row0);
+      bulk_commit();
+    }
+    ew.cur ^= 1;
+  }
+  float* slot = red + (parity * 2 + half) * 128;
+  slot[row] = ss;
+  named_barrier(1 + quarter, 64);
+  if (half == 0 && valid) {
+    const float total = slot[row] + red[(parity * 2 + 1) * 128 + row];
+    args.row_inv_out[R] = 16.0f / sqrtf(total + 1.0e-12f);   // sqrtf(256) / sqrtf(sum + 1e-12)
+  }
+}
+
+// ---------------------------------------------------------------- direct per-row epilogues
+// Grouped mask layers, the QKV gate tile and the fp32 test store.
+template <typename T, int EPI>
+__device__ __forceinline__ void epilogue_direct(const GemmArgs& args, const TileInfo& ti, uint32_t taddr, int half,
+                                                long long R, bool valid) {
+  const float inv = (args.row_inv != nullptr && valid) ? __ldg(args.row_inv + R) : 1.0f;
+  const int c_end = min(ti.n_size, half * 128 + 128);
+  for (int c = half * 128; c < c_end; c += 32) {
+    float v[32];
+    int count;
+    if (ti.n_size - c >= 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c, r);
+      tmem_wait_ld();
+      reg_fence(r);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      count = 32;
     } else {
-      float* dst = static_cast<float*>(args.out) +
-                   ((chunk * args.frames + t) * kFreqBins + first) * 4 + p0;
+      uint32_t r[16];
+      tmem_ld16(taddr + c, r);
+      tmem_wait_ld();
+      reg_fence(r);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int p = p0 + j;
-        if (2 * j < count && p < dim) {
-          const float value = v[2 * j] + __ldg(bias + 2 * j);
-          const float gate = v[2 * j + 1] + __ldg(bias + 2 * j + 1);
-          dst[j] = value * sigmoidf(gate);
+      for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+#pragma unroll
+      for (int j = 16; j < 32; ++j) v[j] = 0.f;
+      count = 16;
+    }
+    if (!valid) continue;
+    const int n = ti.n0 + c;
+    if (EPI == kEpiQkvRope) {
+      // Gate tile: columns 0..7 are the 8 head-gate logits of the normed row
+      // (gates :853, sigmoid in apply_gates :808-818).
+      float4 g0, g1;
+      g0.x = sigmoidf(v[0] * inv + __ldg(args.gate_b + 0));
+      g0.y = sigmoidf(v[1] * inv + __ldg(args.gate_b + 1));
+      g0.z = sigmoidf(v[2] * inv + __ldg(args.gate_b + 2));
+      g0.w = sigmoidf(v[3] * inv + __ldg(args.gate_b + 3));
+      g1.x = sigmoidf(v[4] * inv + __ldg(args.gate_b + 4));
+      g1.y = sigmoidf(v[5] * inv + __ldg(args.gate_b + 5));
+      g1.z = sigmoidf(v[6] * inv + __ldg(args.gate_b + 6));
+      g1.w = sigmoidf(v[7] * inv + __ldg(args.gate_b + 7));
+      reinterpret_cast<float4*>(args.gates_out + R * kHeads)[0] = g0;
+      reinterpret_cast<float4*>(args.gates_out + R * kHeads)[1] = g1;
+    } else if (EPI == kEpiTanhBand) {
+      const float* bias = args.bias + ti.b_row + c;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j] * inv + __ldg(bias + j));
+      store_row16<T>(static_cast<T*>(args.out) + R * args.ldo + n, v, count);
+    } else if (EPI == kEpiStoreF32) {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(args.out) + R * args.ldo + n);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q * 4 < count) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else if (EPI == kEpiGluMask) {
+      // Columns hold interleaved (value, gate) pairs of band `ti.band`; pair p
+      // is mask component p of the band: frequency first + p/4, channel
+      // (p/2)%2, re/im p%2 (mask_band, vocalarc_separation.c:1330-1338).
+      const int band = ti.band;
+      const int dim = c_band_dim[band];
+      const int first = c_band_first[band];
+      const long long seq = R / args.frames;
+      const int t = static_cast<int>(R - seq * args.frames);
+      const long long chunk = seq / kBands;
+      const float* bias = args.bias + ti.b_row + c;
+      const int p0 = n >> 1;
+      if (args.mask_ref_layout) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int p = p0 + j;
+          if (2 * j < count && p < dim) {
+            const float value = v[2 * j] + __ldg(bias + 2 * j);
+            const float gate = v[2 * j + 1] + __ldg(bias + 2 * j + 1);
+            const int f = first + (p >> 2), ch = (p >> 1) & 1, ri = p & 1;
+            float* dst = static_cast<float*>(args.out) +
+                         ((static_cast<long long>(f) * kChannels + ch) * args.frames + t) * 2 + ri;
+            *dst = value * sigmoidf(gate);
+          }
+        }
+      } else {
+        float* dst = static_cast<float*>(args.out) + ((chunk * args.frames + t) * kFreqBins + first) * 4 + p0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int p = p0 + j;
+          if (2 * j < count && p < dim) {
+            const float value = v[2 * j] + __ldg(bias + 2 * j);
+            const float gate = v[2 * j + 1] + __ldg(bias + 2 * j + 1);
+            dst[j] = value * sigmoidf(gate);
+          }
         }
       }
     }
@@ -204,17 +412,21 @@ __device__ __forceinline__ bool wait_no_abort_check(uint64_t* bar, uint32_t pari
 template <typename T, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_d,
                 const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);
+  uint8_t* sEpi = sB + kStages * kBBytes;
+  float* red = reinterpret_cast<float*>(sEpi + kEpiWarps * 2 * kStageBuf);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + kRedBytes);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* ep_bar = drain + 1;   // [8 warps][2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_bar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -230,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&ep_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -325,6 +538,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
+    const int ew_index = warp - 2;
+    EpiWarp ew;
+    ew.buf[0] = sEpi + ew_index * 2 * kStageBuf;
+    ew.buf[1] = ew.buf[0] + kStageBuf;
+    ew.bar[0] = &ep_bar[ew_index * 2];
+    ew.bar[1] = &ep_bar[ew_index * 2 + 1];
+    ew.phase[0] = ew.phase[1] = 0;
+    ew.cur = 0;
+    ew.lane = lane;
     int it = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
@@ -335,44 +557,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
       const long long R = static_cast<long long>(ti.a_row) + row;
       const bool valid = row < ti.m_valid;
-      // A 32-column chunk of this half always starts at column 32*half of a
-      // 64-wide head, so it uses RoPE pairs [16*half, 16*half + 16) of the
-      // row's position: load them once per tile.
-      float4 rope[8];
-      if (EPI == kEpiQkvRope) {
-        const int pos = static_cast<int>((R / args.pos_div) % args.pos_mod);
-        const float4* table = reinterpret_cast<const float4*>(args.rope + static_cast<long long>(pos) * (kDimHead / 2) + 16 * half);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) rope[i] = valid && ti.n0 < args.rope_cols ? __ldg(table + i) : make_float4(1.f, 0.f, 1.f, 0.f);
-      }
-      for (int c = half * 32; c < ti.n_size; c += 64) {
-        float v[32];
-        int count;
-        if (ti.n_size - c >= 32) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c, r);
-          tmem_wait_ld();
-          reg_fence(r);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          count = 32;
-        } else {
-          uint32_t r[16];
-          tmem_ld16(taddr + c, r);
-          tmem_wait_ld();
-          reg_fence(r);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-#pragma unroll
-          for (int j = 16; j < 32; ++j) v[j] = 0.f;
-          count = 16;
-        }
-        if (valid) epilogue_chunk<T, EPI>(args, ti, R, c, v, count, rope);
+      const int row0 = ti.a_row + quarter * 32;
+      if (EPI == kEpiResidual) {
+        epilogue_residual<T>(args, &map_c, &map_d, ti, ew, taddr, half, quarter, row, R, valid, row0, it & 1, red);
+      } else if ((EPI == kEpiStore || EPI == kEpiGelu || EPI == kEpiQkvRope) && ti.n_size == kBN) {
+        epilogue_out16<T, EPI>(args, &map_c, ti, ew, taddr, half, row, R, valid, row0);
+      } else {
+        epilogue_direct<T, EPI>(args, ti, taddr, half, R, valid);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
+    if (lane == 0) bulk_wait_all();   // outstanding tensor stores complete before exit
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -384,42 +582,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <typename T, int EPI>
-cudaError_t launch_typed(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmArgs& args,
-                         int sm_count, cudaStream_t stream) {
+cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& args, int sm_count, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   if (args.num_tiles <= 0) return cudaSuccess;
   const int grid = args.num_tiles < sm_count ? args.num_tiles : sm_count;
-  gemm_kernel<T, EPI><<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, args);
+  gemm_kernel<T, EPI><<<grid, kThreads, kSmemBytes, stream>>>(maps.a, maps.b, maps.c, maps.d, args);
   return cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t dispatch(int epilogue, const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int sms,
-                     cudaStream_t s) {
+cudaError_t dispatch(int epilogue, const GemmMaps& m, const GemmArgs& args, int sms, cudaStream_t s) {
   switch (epilogue) {
-    case kEpiStore: return launch_typed<T, kEpiStore>(a, b, args, sms, s);
-    case kEpiGelu: return launch_typed<T, kEpiGelu>(a, b, args, sms, s);
-    case kEpiQkvRope: return launch_typed<T, kEpiQkvRope>(a, b, args, sms, s);
-    case kEpiResidual: return launch_typed<T, kEpiResidual>(a, b, args, sms, s);
-    case kEpiTanhBand: return launch_typed<T, kEpiTanhBand>(a, b, args, sms, s);
-    case kEpiGluMask: return launch_typed<T, kEpiGluMask>(a, b, args, sms, s);
-    case kEpiStoreF32: return launch_typed<T, kEpiStoreF32>(a, b, args, sms, s);
+    case kEpiStore: return launch_typed<T, kEpiStore>(m, args, sms, s);
+    case kEpiGelu: return launch_typed<T, kEpiGelu>(m, args, sms, s);
+    case kEpiQkvRope: return launch_typed<T, kEpiQkvRope>(m, args, sms, s);
+    case kEpiResidual: return launch_typed<T, kEpiResidual>(m, args, sms, s);
+    case kEpiTanhBand: return launch_typed<T, kEpiTanhBand>(m, args, sms, s);
+    case kEpiGluMask: return launch_typed<T, kEpiGluMask>(m, args, sms, s);
+    case kEpiStoreF32: return launch_typed<T, kEpiStoreF32>(m, args, sms, s);
     default: return cudaErrorInvalidValue;
   }
 }
 
 }  // namespace
 
-cudaError_t launch_gemm(int epilogue, bool bf16, const CUtensorMap& map_a, const CUtensorMap& map_b,
-                        const GemmArgs& args, int sm_count, cudaStream_t stream) {
-  return bf16 ? dispatch<__nv_bfloat16>(epilogue, map_a, map_b, args, sm_count, stream)
-              : dispatch<__half>(epilogue, map_a, map_b, args, sm_count, stream);
+cudaError_t launch_gemm(int epilogue, bool bf16, const GemmMaps& maps, const GemmArgs& args, int sm_count,
+                        cudaStream_t stream) {
+  return bf16 ? dispatch<__nv_bfloat16>(epilogue, maps, args, sm_count, stream)
+              : dispatch<__half>(epilogue, maps, args, sm_count, stream);
 }
 
 cudaError_t upload_band_tables(const int* first, const int* dims) {

@@ -8,8 +8,10 @@
 // kernel addresses a sequence (a band over time, or a frame over bands)
 // through a 4-D TMA tensor map, so the reference's transpose kernels
 // (native_gpu_cuda.cu:428-451) disappear.  16-bit copies feed the tensor
-// cores (normed rows, q/k/v, gated attention, FFN hidden); the mask head reads
-// the band-major rows directly as its per-band A operand.
+// cores (x, q/k/v, gated attention, FFN hidden); the mask head reads the
+// band-major rows directly as its per-band A operand.  Every RMSNorm gamma is
+// folded into the weights of the GEMM that consumes the norm, and the GEMM
+// that updates x writes the per-row factor sqrt(256)/|x| next to x16.
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -93,14 +95,15 @@ struct DeviceBuffer {
   size_t bytes = 0;
 };
 
+// Device weights of one axial block.  qkv holds 1552 rows: the 1536 q|k|v
+// rows and the 8 head-gate rows, both scaled column-wise by the attention
+// RMSNorm gamma, then 8 zero rows; ff1 is scaled by the FF RMSNorm gamma.
+constexpr int kQkvRows = kQkvDim + 16;
 struct BlockW {
   void* qkv = nullptr;
   void* out = nullptr;
   void* ff1 = nullptr;
   void* ff2 = nullptr;
-  float* gamma = nullptr;
-  float* ff_gamma = nullptr;
-  float* gate_w = nullptr;
   float* gate_b = nullptr;
   float* ff1_b = nullptr;
   float* ff2_b = nullptr;
@@ -120,7 +123,6 @@ struct MaskW {
   float* b1 = nullptr;
   void* w2 = nullptr;
   float* b2 = nullptr;
-  float* final_gamma = nullptr;
   int w2_off[kBands];
   int w2_rows[kBands];
   int w2_total = 0;
@@ -166,7 +168,9 @@ struct native_gpu {
   long long ws_tokens = 0;
   float* x = nullptr;
   float* x_alt = nullptr;
-  void* normed = nullptr;
+  void* x16 = nullptr;          // 16-bit copy of x (A operand of the norm-folded GEMMs)
+  float* row_inv = nullptr;     // per-row sqrt(256)/|x| of the current x
+  int stats_valid = 0;          // x16 / row_inv describe the current x
   void* qkv = nullptr;
   void* attn = nullptr;
   float* gates = nullptr;
@@ -270,7 +274,8 @@ bool ensure_tokens(native_gpu* g, long long tokens) {
   g->ws_tokens = 0;
   const size_t t = static_cast<size_t>(tokens);
   if (!grow(g, &g->x, t * kDim * 4, "cudaMalloc(x)") || !grow(g, &g->x_alt, t * kDim * 4, "cudaMalloc(x_alt)") ||
-      !grow(g, &g->normed, t * kDim * 2, "cudaMalloc(normed)") ||
+      !grow(g, &g->x16, t * kDim * 2, "cudaMalloc(x16)") ||
+      !grow(g, &g->row_inv, t * 4, "cudaMalloc(row_inv)") ||
       !grow(g, &g->qkv, t * kQkvDim * 2, "cudaMalloc(qkv)") ||
       !grow(g, &g->attn, t * kDimInner * 2, "cudaMalloc(attn)") ||
       !grow(g, &g->gates, t * kHeads * 4, "cudaMalloc(gates)"))
@@ -330,17 +335,37 @@ bool ensure_rope(native_gpu* g, int positions) {
   return true;
 }
 
+// GEMM operand map: 16-bit [rows][k], box 64 x box_rows, 128-byte swizzle.
 bool make_map_rows(native_gpu* g, CUtensorMap* map, const void* base, long long rows, int k, int box_rows) {
-  (void)g;
   return make_tmap_2d(map, base, 2, static_cast<uint64_t>(k), static_cast<uint64_t>(rows),
-                      static_cast<uint64_t>(k) * 2, 64, static_cast<uint32_t>(box_rows), true, g->bf16 != 0);
+                      static_cast<uint64_t>(k) * 2, 64, static_cast<uint32_t>(box_rows), 128, g->bf16 != 0);
+}
+
+// Staged-epilogue maps: 16-bit [rows][n] stores in 64 x 32 boxes; fp32 residual
+// [rows][256] in 32 x 32 boxes; its 16-bit copy in 32 x 32 boxes (64B swizzle).
+bool make_out16_map(native_gpu* g, CUtensorMap* map, const void* base, long long rows, int n) {
+  return make_tmap_2d(map, base, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(rows),
+                      static_cast<uint64_t>(n) * 2, 64, 32, 128, g->bf16 != 0);
+}
+bool make_resid_maps(native_gpu* g, GemmMaps& maps, long long rows) {
+  return make_tmap_2d(&maps.c, g->x, 4, kDim, static_cast<uint64_t>(rows), kDim * 4ull, 32, 32, 128, false) &&
+         make_tmap_2d(&maps.d, g->x16, 2, kDim, static_cast<uint64_t>(rows), kDim * 2ull, 32, 32, 64, g->bf16 != 0);
+}
+
+// Scales column i of W[out][in] by scale[i] (an RMSNorm gamma folded into the
+// GEMM that consumes the norm).
+void scale_columns(std::vector<float>& w, int in, const float* scale) {
+  const size_t rows = w.size() / static_cast<size_t>(in);
+  for (size_t r = 0; r < rows; ++r)
+    for (int i = 0; i < in; ++i) w[r * in + i] *= scale[i];
 }
 
 bool upload16(native_gpu* g, Arena& arena, const float* packed, int in, int out, void** dst, CUtensorMap* map,
-              int box_rows) {
+              int box_rows, const float* col_scale = nullptr) {
   std::vector<float> w;
   std::vector<uint16_t> h;
   unpack_packed(packed, in, out, w);
+  if (col_scale != nullptr) scale_columns(w, in, col_scale);
   to16(w, g->bf16 != 0, h);
   *dst = arena.take(h.size() * 2);
   if (*dst == nullptr) return false;
@@ -354,20 +379,29 @@ bool upload_f32(native_gpu* g, Arena& arena, const float* src, size_t count, flo
   return cuda_ok(g, cudaMemcpy(*dst, src, count * 4, cudaMemcpyHostToDevice), "upload vector");
 }
 
-constexpr size_t kBlockBytes = (static_cast<size_t>(kQkvDim) * kDim + kDim * kDimInner + 2 * kFfDim * kDim) * 2 +
-                               (kHeads * kDim + 3 * kDim + kHeads + kFfDim) * 4 + 16 * 1024;
+constexpr size_t kBlockBytes = (static_cast<size_t>(kQkvRows) * kDim + kDim * kDimInner + 2 * kFfDim * kDim) * 2 +
+                               (kHeads + kFfDim + kDim) * 4 + 16 * 1024;
 
 bool upload_block(native_gpu* g, Arena& arena, const native_gpu_transformer_weights& w, BlockW& b) {
-  std::vector<float> gw;
-  if (!upload16(g, arena, w.qkv, kDim, kQkvDim, &b.qkv, &b.m_qkv, 256) ||
-      !upload16(g, arena, w.out_weight, kDimInner, kDim, &b.out, &b.m_out, 256) ||
-      !upload16(g, arena, w.ff1_weight, kDim, kFfDim, &b.ff1, &b.m_ff1, 256) ||
+  // q|k|v rows, then the gate rows, then zero rows; all scaled by the attention gamma.
+  std::vector<float> qkv, gw;
+  unpack_packed(w.qkv, kDim, kQkvDim, qkv);
+  unpack_packed(w.gate_weight, kDim, kHeads, gw);
+  qkv.resize(static_cast<size_t>(kQkvRows) * kDim, 0.f);
+  std::copy(gw.begin(), gw.end(), qkv.begin() + static_cast<size_t>(kQkvDim) * kDim);
+  scale_columns(qkv, kDim, w.gamma);
+  std::vector<uint16_t> h;
+  to16(qkv, g->bf16 != 0, h);
+  b.qkv = arena.take(h.size() * 2);
+  if (b.qkv == nullptr || !cuda_ok(g, cudaMemcpy(b.qkv, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "qkv"))
+    return false;
+  if (!make_map_rows(g, &b.m_qkv, b.qkv, kQkvRows, kDim, 256)) return false;
+  if (!upload16(g, arena, w.out_weight, kDimInner, kDim, &b.out, &b.m_out, 256) ||
+      !upload16(g, arena, w.ff1_weight, kDim, kFfDim, &b.ff1, &b.m_ff1, 256, w.ff_gamma) ||
       !upload16(g, arena, w.ff2_weight, kFfDim, kDim, &b.ff2, &b.m_ff2, 256))
     return false;
-  unpack_packed(w.gate_weight, kDim, kHeads, gw);
-  return upload_f32(g, arena, gw.data(), gw.size(), &b.gate_w) && upload_f32(g, arena, w.gamma, kDim, &b.gamma) &&
-         upload_f32(g, arena, w.ff_gamma, kDim, &b.ff_gamma) && upload_f32(g, arena, w.gate_bias, kHeads, &b.gate_b) &&
-         upload_f32(g, arena, w.ff1_bias, kFfDim, &b.ff1_b) && upload_f32(g, arena, w.ff2_bias, kDim, &b.ff2_b);
+  return upload_f32(g, arena, w.gate_bias, kHeads, &b.gate_b) && upload_f32(g, arena, w.ff1_bias, kFfDim, &b.ff1_b) &&
+         upload_f32(g, arena, w.ff2_bias, kDim, &b.ff2_b);
 }
 
 int mask_w2_rows_total() {
@@ -389,6 +423,7 @@ bool upload_mask(native_gpu* g, Arena& arena, const native_gpu_mask_band* bands,
   std::vector<float> w, all1(static_cast<size_t>(kBands) * kFfDim * kDim), b1(static_cast<size_t>(kBands) * kFfDim);
   for (int b = 0; b < kBands; ++b) {
     unpack_packed(bands[b].first_weight, kDim, kFfDim, w);
+    scale_columns(w, kDim, final_gamma);   // the final RMSNorm gamma, folded
     memcpy(&all1[static_cast<size_t>(b) * kFfDim * kDim], w.data(), w.size() * 4);
     memcpy(&b1[static_cast<size_t>(b) * kFfDim], bands[b].first_bias, kFfDim * 4);
   }
@@ -420,8 +455,7 @@ bool upload_mask(native_gpu* g, Arena& arena, const native_gpu_mask_band* bands,
   if (m.w2 == nullptr || !cuda_ok(g, cudaMemcpy(m.w2, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "mask w2"))
     return false;
   if (!make_map_rows(g, &m.m_w2, m.w2, m.w2_total, kFfDim, 16)) return false;
-  if (!upload_f32(g, arena, b2.data(), b2.size(), &m.b2)) return false;
-  return upload_f32(g, arena, final_gamma, kDim, &m.final_gamma);
+  return upload_f32(g, arena, b2.data(), b2.size(), &m.b2);
 }
 
 bool ensure_mask_tiles(native_gpu* g, int frames, const MaskW& m) {
@@ -469,22 +503,38 @@ struct AxisPlan {
   int pos_dim, d1, d2, d3, sequences, length, pos_div, pos_mod;
 };
 
+bool ensure_stats(native_gpu* g, long long tokens, int remap_s0 = 0, int remap_l0 = 0) {
+  if (g->stats_valid && remap_s0 == 0) return true;
+  if (!launched(g, launch_row_stats(g->x, tokens, g->x16, g->row_inv, g->bf16 != 0, remap_s0, remap_l0, g->stream),
+                "row stats"))
+    return false;
+  g->stats_valid = remap_s0 == 0;
+  return true;
+}
+
+// One axial block on the residual stream g->x (transformer_forward,
+// vocalarc_separation.c:836-873).  Needs x16 / row_inv of the current x; leaves
+// them valid for the updated x.
 bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan& ax) {
   const bool bf = g->bf16 != 0;
-  if (!ensure_rope(g, ax.length)) return false;
-  if (!launched(g, launch_norm(g->x, tokens, w.gamma, w.gate_w, w.gate_b, g->normed, g->gates, bf, 0, 0, g->stream),
-                "norm+gates"))
+  if (!ensure_rope(g, ax.length) || !ensure_stats(g, tokens)) return false;
+  GemmMaps maps;
+  // q|k|v = RoPE(inv * x16 (gamma o Wqkv)^T), gates = sigmoid(inv * x16 (gamma o Wg)^T + b)
+  if (!make_map_rows(g, &maps.a, g->x16, tokens, kDim, 128) || !make_out16_map(g, &maps.c, g->qkv, tokens, kQkvDim))
     return false;
-  CUtensorMap a;
+  maps.b = w.m_qkv;
+  maps.d = maps.c;
   GemmArgs args = uniform_args(g, tokens, kQkvDim, kDim);
-  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
-  args.out = g->qkv;
-  args.ldo = kQkvDim;
+  args.gate_tile = 1;
+  args.num_tiles = static_cast<int>((tokens + 127) / 128) * (args.n_tiles + 1);
+  args.row_inv = g->row_inv;
   args.rope = g->d_rope;
   args.pos_div = ax.pos_div;
   args.pos_mod = ax.pos_mod;
   args.rope_cols = 2 * kDimInner;
-  if (!launched(g, launch_gemm(kEpiQkvRope, bf, a, w.m_qkv, args, g->sm_count, g->stream), "qkv gemm")) return false;
+  args.gate_b = w.gate_b;
+  args.gates_out = g->gates;
+  if (!launched(g, launch_gemm(kEpiQkvRope, bf, maps, args, g->sm_count, g->stream), "qkv gemm")) return false;
 
   CUtensorMap q4;
   const uint64_t dims[4] = {static_cast<uint64_t>(kQkvDim), static_cast<uint64_t>(ax.d1),
@@ -506,42 +556,47 @@ bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan&
   if (!launched(g, launch_attention(bf, q4, at, g->stream), ax.length <= 128 ? "attention (L<=128)" : "attention (L>128)"))
     return false;
 
-  if (!make_map_rows(g, &a, g->attn, tokens, kDimInner, 128)) return false;
+  // x += out(attn); x16 and row_inv of the new x
+  if (!make_map_rows(g, &maps.a, g->attn, tokens, kDimInner, 128) || !make_resid_maps(g, maps, tokens)) return false;
+  maps.b = w.m_out;
   args = uniform_args(g, tokens, kDim, kDimInner);
-  args.resid = g->x;
-  args.ldr = kDim;
-  if (!launched(g, launch_gemm(kEpiResidual, bf, a, w.m_out, args, g->sm_count, g->stream), "out gemm")) return false;
+  args.row_inv_out = g->row_inv;
+  if (!launched(g, launch_gemm(kEpiResidual, bf, maps, args, g->sm_count, g->stream), "out gemm")) return false;
 
-  if (!launched(g, launch_norm(g->x, tokens, w.ff_gamma, nullptr, nullptr, g->normed, nullptr, bf, 0, 0, g->stream),
-                "ff norm"))
+  // hidden = GELU(inv * x16 (ff_gamma o W1)^T + b1)
+  if (!make_map_rows(g, &maps.a, g->x16, tokens, kDim, 128) || !make_out16_map(g, &maps.c, g->qkv, tokens, kFfDim))
     return false;
-  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
+  maps.b = w.m_ff1;
+  maps.d = maps.c;
   args = uniform_args(g, tokens, kFfDim, kDim);
-  args.out = g->qkv;
-  args.ldo = kFfDim;
+  args.row_inv = g->row_inv;
   args.bias = w.ff1_b;
-  if (!launched(g, launch_gemm(kEpiGelu, bf, a, w.m_ff1, args, g->sm_count, g->stream), "ff1 gemm")) return false;
-  if (!make_map_rows(g, &a, g->qkv, tokens, kFfDim, 128)) return false;
+  if (!launched(g, launch_gemm(kEpiGelu, bf, maps, args, g->sm_count, g->stream), "ff1 gemm")) return false;
+
+  // x += hidden W2^T + b2; x16 and row_inv of the new x
+  if (!make_map_rows(g, &maps.a, g->qkv, tokens, kFfDim, 128) || !make_resid_maps(g, maps, tokens)) return false;
+  maps.b = w.m_ff2;
   args = uniform_args(g, tokens, kDim, kFfDim);
-  args.resid = g->x;
-  args.ldr = kDim;
   args.bias = w.ff2_b;
-  return launched(g, launch_gemm(kEpiResidual, bf, a, w.m_ff2, args, g->sm_count, g->stream), "ff2 gemm");
+  args.row_inv_out = g->row_inv;
+  if (!launched(g, launch_gemm(kEpiResidual, bf, maps, args, g->sm_count, g->stream), "ff2 gemm")) return false;
+  g->stats_valid = 1;
+  return true;
 }
 
-// Final RMSNorm + mask MLPs over `segments` x 90 x frames band-major tokens.
-// remap: physical [frames][90] rows are re-ordered band-major by the norm.
+// Final RMSNorm (gamma folded into the first mask layer) + mask MLPs over
+// `segments` x 90 x frames band-major tokens.  frame_major_rows: the physical
+// rows are [frames][90] and the row statistics are written band-major.
 bool run_mask(native_gpu* g, const MaskW& m, int segments, int frames, bool frame_major_rows, bool ref_layout,
               float* mask_out) {
   const bool bf = g->bf16 != 0;
   const long long tokens = static_cast<long long>(segments) * kBands * frames;
-  if (!launched(g, launch_norm(g->x, tokens, m.final_gamma, nullptr, nullptr, g->normed, nullptr, bf,
-                               frame_major_rows ? frames : 0, frame_major_rows ? kBands : 0, g->stream),
-                "final norm"))
-    return false;
+  if (!ensure_stats(g, tokens, frame_major_rows ? frames : 0, frame_major_rows ? kBands : 0)) return false;
   if (!ensure_mask_tiles(g, frames, m)) return false;
-  CUtensorMap a;
-  if (!make_map_rows(g, &a, g->normed, tokens, kDim, 128)) return false;
+  GemmMaps maps;
+  if (!make_map_rows(g, &maps.a, g->x16, tokens, kDim, 128)) return false;
+  maps.b = m.m_w1;
+  maps.c = maps.d = maps.a;
   GemmArgs args;
   memset(&args, 0, sizeof(args));
   args.k_blocks = kDim / 64;
@@ -552,10 +607,12 @@ bool run_mask(native_gpu* g, const MaskW& m, int segments, int frames, bool fram
   args.out = g->qkv;
   args.ldo = kFfDim;
   args.bias = m.b1;
+  args.row_inv = g->row_inv;
   args.err = g->d_err;
   args.pos_div = args.pos_mod = 1;
-  if (!launched(g, launch_gemm(kEpiTanhBand, bf, a, m.m_w1, args, g->sm_count, g->stream), "mask gemm 1")) return false;
-  if (!make_map_rows(g, &a, g->qkv, tokens, kFfDim, 128)) return false;
+  if (!launched(g, launch_gemm(kEpiTanhBand, bf, maps, args, g->sm_count, g->stream), "mask gemm 1")) return false;
+  if (!make_map_rows(g, &maps.a, g->qkv, tokens, kFfDim, 128)) return false;
+  maps.b = m.m_w2;
   args.k_blocks = kFfDim / 64;
   args.tiles = g->d_tiles2;
   args.tiles_per_chunk = g->n_tiles2;
@@ -564,9 +621,10 @@ bool run_mask(native_gpu* g, const MaskW& m, int segments, int frames, bool fram
   args.out = mask_out;
   args.ldo = 0;
   args.bias = m.b2;
+  args.row_inv = nullptr;
   args.frames = frames;
   args.mask_ref_layout = ref_layout ? 1 : 0;
-  return launched(g, launch_gemm(kEpiGluMask, bf, a, m.m_w2, args, g->sm_count, g->stream), "mask gemm 2");
+  return launched(g, launch_gemm(kEpiGluMask, bf, maps, args, g->sm_count, g->stream), "mask gemm 2");
 }
 
 AxisPlan time_axis(int segments, int frames) {
@@ -587,6 +645,7 @@ bool forward_segments(native_gpu* g, const float* d_audio, const SegmentMap& map
                                      g->band.gamma_off, g->band.bias, g->x, g->stream),
                 "band split"))
     return false;
+  g->stats_valid = 0;
   for (int layer = 0; layer < kDepth; ++layer) {
     if (!run_block(g, g->blocks[layer][0], tokens, time_axis(segments, frames))) return false;
     if (!run_block(g, g->blocks[layer][1], tokens, band_axis(segments, frames))) return false;
@@ -790,7 +849,7 @@ void native_gpu_destroy(native_gpu* g) {
   if (g == nullptr) return;
   cudaSetDevice(g->device);
   if (g->stream != nullptr) cudaStreamSynchronize(g->stream);
-  void* ptrs[] = {g->x, g->x_alt, g->normed, g->qkv, g->attn, g->gates, g->spec, g->mask, g->frames_buf,
+  void* ptrs[] = {g->x, g->x_alt, g->x16, g->row_inv, g->qkv, g->attn, g->gates, g->spec, g->mask, g->frames_buf,
                   g->seg_out, g->audio_in, g->audio_out, g->d_tiles1, g->d_tiles2, g->d_err, g->d_window,
                   g->d_twiddle, g->d_rope, g->abi_mask_mem};
   for (void* p : ptrs)
@@ -841,6 +900,7 @@ int native_gpu_transformer(native_gpu* g, int sequences, int length, float* data
   if (w == nullptr) return 0;
   if (!cuda_ok(g, cudaMemcpyAsync(g->x, data, tokens * kDim * 4, cudaMemcpyHostToDevice, g->stream), "H2D data"))
     return 0;
+  g->stats_valid = 0;
   AxisPlan ax{1, length, sequences, 1, sequences, length, 1, length};
   if (!run_block(g, *w, tokens, ax)) return 0;
   if (!cuda_ok(g, cudaMemcpyAsync(data, g->x, tokens * kDim * 4, cudaMemcpyDeviceToHost, g->stream), "D2H data"))
@@ -855,6 +915,7 @@ int native_gpu_resident_begin(native_gpu* g, int sequences, int length, const fl
   if (!ensure_tokens(g, tokens)) return 0;
   if (!cuda_ok(g, cudaMemcpyAsync(g->x, data, tokens * kDim * 4, cudaMemcpyHostToDevice, g->stream), "H2D begin"))
     return 0;
+  g->stats_valid = 0;
   if (!sync_and_check(g, "resident begin")) return 0;
   g->resident_active = 1;
   g->resident_tokens = tokens;
@@ -1158,13 +1219,19 @@ int vocalarc_b200_stage_gemm(native_gpu* g, int epilogue, const void* a, const v
   if (!active(g) || m <= 0 || n <= 0 || n % 256 != 0 || k <= 0 || k % 64 != 0) return 0;
   if (epilogue != kEpiStore && epilogue != kEpiGelu && epilogue != kEpiStoreF32) return 0;
   cudaSetDevice(g->device);
-  CUtensorMap ma, mb;
-  if (!make_map_rows(g, &ma, a, m, k, 128) || !make_map_rows(g, &mb, b, n, k, 256)) return 0;
+  GemmMaps maps;
+  if (!make_map_rows(g, &maps.a, a, m, k, 128) || !make_map_rows(g, &maps.b, b, n, k, 256)) return 0;
+  if (epilogue == kEpiStoreF32)
+    maps.c = maps.d = maps.a;
+  else if (!make_out16_map(g, &maps.c, out, m, n))
+    return 0;
+  else
+    maps.d = maps.c;
   GemmArgs args = uniform_args(g, m, n, k);
   args.out = out;
   args.ldo = n;
   args.bias = bias;
-  return launched(g, launch_gemm(epilogue, g->bf16 != 0, ma, mb, args, g->sm_count, g->stream), "stage gemm") ? 1 : 0;
+  return launched(g, launch_gemm(epilogue, g->bf16 != 0, maps, args, g->sm_count, g->stream), "stage gemm") ? 1 : 0;
 }
 
 int vocalarc_b200_stage_attention(native_gpu* g, const void* qkv, const float* gates, void* out, int d1, int d2,
@@ -1235,6 +1302,7 @@ int vocalarc_b200_stage_block(native_gpu* g, float* x, int segments, int frames,
   const long long tokens = static_cast<long long>(segments) * kBands * frames;
   if (!ensure_tokens(g, tokens)) return 0;
   if (!cuda_ok(g, cudaMemcpyAsync(g->x, x, tokens * kDim * 4, cudaMemcpyDeviceToDevice, g->stream), "D2D")) return 0;
+  g->stats_valid = 0;
   if (!run_block(g, g->blocks[layer][axis], tokens, axis == 0 ? time_axis(segments, frames) : band_axis(segments, frames)))
     return 0;
   return cuda_ok(g, cudaMemcpyAsync(x, g->x, tokens * kDim * 4, cudaMemcpyDeviceToDevice, g->stream), "D2D") ? 1 : 0;
@@ -1246,6 +1314,7 @@ int vocalarc_b200_stage_mask(native_gpu* g, const float* x, int segments, int fr
   const long long tokens = static_cast<long long>(segments) * kBands * frames;
   if (!ensure_tokens(g, tokens)) return 0;
   if (!cuda_ok(g, cudaMemcpyAsync(g->x, x, tokens * kDim * 4, cudaMemcpyDeviceToDevice, g->stream), "D2D")) return 0;
+  g->stats_valid = 0;
   return run_mask(g, g->maskw, segments, frames, false, false, mask) ? 1 : 0;
 }
 

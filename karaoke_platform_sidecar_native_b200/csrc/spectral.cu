@@ -7,9 +7,8 @@
 //    double-precision twiddles, checked against the oracle by SNR.
 //  * band_split_kernel: per band gather + RMSNorm + Linear(d_b -> 256) + bias
 //    (band_split_one :887-915), fp32 SIMT; writes the band-major token layout.
-//  * norm_kernel: RMSNorm (+ optional head-gate projection and sigmoid) to a
-//    16-bit copy for the next tensor-core GEMM (rms_norm_row :419-424,
-//    gates :853 / apply_gates :808-818).
+//  * row_stats_kernel: 16-bit copy of the residual and its per-row RMSNorm
+//    factor for the norm-folded GEMMs (rms_norm_row :419-424).
 //  * istft_frames_kernel / overlap_add_kernel: complex mask, Hermitian
 //    inverse real FFT, window, overlap-add in frame order, divide by the
 //    window envelope or 0 when it is <= 1e-12 (istft_channels :1084-1127).
@@ -180,67 +179,35 @@ __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict
     if (t0 + tt < frames) out[static_cast<long long>(t0 + tt) * kDim] = acc[tt];
 }
 
-// ---------------------------------------------------------------- RMSNorm (+ gates)
+// ---------------------------------------------------------------- row statistics
+// x16 = 16-bit copy of x, inv = sqrt(256) / sqrt(sum x^2 + 1e-12) per row (the
+// scale of rms_norm_row_scalar, vocalarc_separation.c:419-424; the gamma is
+// folded into the consuming GEMM's weights).  One warp per 256-wide row.
 template <typename T>
-__global__ void __launch_bounds__(256) norm_kernel(const float* __restrict__ x, long long rows,
-                                                   const float* __restrict__ gamma,
-                                                   const float* __restrict__ gate_w, const float* __restrict__ gate_b,
-                                                   T* __restrict__ normed, float* __restrict__ gates, int remap_s0,
-                                                   int remap_l0) {
+__global__ void __launch_bounds__(256) row_stats_kernel(const float* __restrict__ x, long long rows,
+                                                        T* __restrict__ x16, float* __restrict__ inv, int remap_s0,
+                                                        int remap_l0) {
   const long long r = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
   const int lane = threadIdx.x & 31;
   const float4* src = reinterpret_cast<const float4*>(x + r * kDim);
-  float v[8];
-  {
-    const float4 a = src[lane];
-    const float4 b = src[32 + lane];
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  const float4 a = src[lane];
+  const float4 b = src[32 + lane];
+  float ss = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float inv = 16.0f / sqrtf(ss + 1.0e-12f);  // sqrtf(256) / sqrtf(sum + 1e-12)
-  const int col0 = lane * 4, col1 = 128 + lane * 4;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[i] = v[i] * inv * __ldg(gamma + col0 + i);
-    v[4 + i] = v[4 + i] * inv * __ldg(gamma + col1 + i);
-  }
   // Optional remap of the token order: physical [s0][l0] -> [l0][s0].
   long long out_row = r;
   if (remap_s0 > 0) out_row = (r % remap_l0) * remap_s0 + r / remap_l0;
-  T* dst = normed + out_row * kDim;
+  T* dst = x16 + out_row * kDim;
   uint2 p0, p1;
-  p0.x = ElemTraits<T>::pack2(v[0], v[1]);
-  p0.y = ElemTraits<T>::pack2(v[2], v[3]);
-  p1.x = ElemTraits<T>::pack2(v[4], v[5]);
-  p1.y = ElemTraits<T>::pack2(v[6], v[7]);
-  *reinterpret_cast<uint2*>(dst + col0) = p0;
-  *reinterpret_cast<uint2*>(dst + col1) = p1;
-  if (gates != nullptr) {
-    float g[kHeads];
-#pragma unroll
-    for (int h = 0; h < kHeads; ++h) {
-      const float* w = gate_w + h * kDim;
-      float s = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s += v[i] * __ldg(w + col0 + i) + v[4 + i] * __ldg(w + col1 + i);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      g[h] = s;
-    }
-    if (lane < kHeads) {
-      float mine = g[0];
-#pragma unroll
-      for (int h = 1; h < kHeads; ++h)
-        if (lane == h) mine = g[h];
-      gates[out_row * kHeads + lane] = 1.0f / (1.0f + __expf(-(mine + gate_b[lane])));
-    }
-  }
+  p0.x = ElemTraits<T>::pack2(a.x, a.y);
+  p0.y = ElemTraits<T>::pack2(a.z, a.w);
+  p1.x = ElemTraits<T>::pack2(b.x, b.y);
+  p1.y = ElemTraits<T>::pack2(b.z, b.w);
+  *reinterpret_cast<uint2*>(dst + lane * 4) = p0;
+  *reinterpret_cast<uint2*>(dst + 128 + lane * 4) = p1;
+  if (lane == 0) inv[out_row] = 16.0f / sqrtf(ss + 1.0e-12f);   // sqrtf(256) / sqrtf(sum + 1e-12)
 }
 
 // ---------------------------------------------------------------- iSTFT
@@ -387,16 +354,16 @@ cudaError_t launch_band_split(const float* spec, int segments, int frames, const
   return cudaGetLastError();
 }
 
-cudaError_t launch_norm(const float* x, long long rows, const float* gamma, const float* gate_w, const float* gate_b,
-                        void* normed, float* gates, bool bf16, int remap_s0, int remap_l0, cudaStream_t stream) {
+cudaError_t launch_row_stats(const float* x, long long rows, void* x16, float* inv, bool bf16, int remap_s0,
+                             int remap_l0, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const long long blocks = (rows + 7) / 8;
   if (bf16)
-    norm_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        x, rows, gamma, gate_w, gate_b, static_cast<__nv_bfloat16*>(normed), gates, remap_s0, remap_l0);
+    row_stats_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        x, rows, static_cast<__nv_bfloat16*>(x16), inv, remap_s0, remap_l0);
   else
-    norm_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        x, rows, gamma, gate_w, gate_b, static_cast<__half*>(normed), gates, remap_s0, remap_l0);
+    row_stats_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        x, rows, static_cast<__half*>(x16), inv, remap_s0, remap_l0);
   return cudaGetLastError();
 }
 

@@ -31,39 +31,24 @@ EncodeTiled encoder() {
 }  // namespace
 
 bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t outer,
-                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128, bool bf16) {
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle_bytes, bool bf16) {
   EncodeTiled fn = encoder();
-  if (fn == nullptr || elem_bytes != 2) return false;
+  if (fn == nullptr || (elem_bytes != 2 && elem_bytes != 4)) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_stride_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    fprintf(stderr, "vocalarc-b200: cuTensorMapEncodeTiled(2d) failed (%d)\n", static_cast<int>(r));
-    return false;
-  }
-  return true;
-}
-
-// Rows r = i2 * d1 + i1 of a [rows][k] 16-bit matrix viewed as (k, d1, d2);
-// the box takes 64 columns of 128 consecutive i2 at one i1.
-bool make_tmap_3d_rows(CUtensorMap* map, const void* base, uint64_t k, uint64_t d1, uint64_t d2, bool bf16) {
-  EncodeTiled fn = encoder();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[3] = {k, d1, d2};
-  const cuuint64_t strides[2] = {k * 2, k * 2 * d1};
-  const cuuint32_t box[3] = {64, 1, 128};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  const CUtensorMapDataType type = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                   : (bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
+  const CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    fprintf(stderr, "vocalarc-b200: cuTensorMapEncodeTiled(3d) failed (%d)\n", static_cast<int>(r));
+    fprintf(stderr, "vocalarc-b200: cuTensorMapEncodeTiled(2d) failed (%d)\n", static_cast<int>(r));
     return false;
   }
   return true;

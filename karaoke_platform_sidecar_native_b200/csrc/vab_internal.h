@@ -26,36 +26,43 @@ constexpr int kBandSplitDim = 4100;  // sum of 4 * band width
 
 // ------------------------------------------------------------------ GEMM
 enum EpilogueKind : int {
-  kEpiStore = 0,      // out_f16[r][n] = acc (+ bias[n])
-  kEpiGelu = 1,       // out_f16[r][n] = gelu(acc + bias[n])
-  kEpiQkvRope = 2,    // out_f16 = acc, RoPE on the q and k columns
-  kEpiResidual = 3,   // resid_f32[r][n] += acc + bias[n]
-  kEpiTanhBand = 4,   // grouped mask layer 1: out_f16[r][n0+c] = tanh(acc + bias[b_row + c])
+  kEpiStore = 0,      // out_16[r][n] = acc * inv[r] (+ bias[n])            (staged TMA store)
+  kEpiGelu = 1,       // out_16[r][n] = gelu(acc * inv[r] + bias[n])         (staged TMA store)
+  kEpiQkvRope = 2,    // out_16 = RoPE(acc * inv[r]) on q and k; gate tile -> sigmoid gates
+  kEpiResidual = 3,   // resid_f32 += acc (+ bias); x16 = resid; row_inv_out = sqrt(256)/|resid|
+  kEpiTanhBand = 4,   // grouped mask layer 1: out_16[r][n0+c] = tanh(acc * inv[r] + bias[b_row + c])
   kEpiGluMask = 5,    // grouped mask layer 2: GLU pairs scattered into the complex mask
   kEpiStoreF32 = 6,   // out_f32[r][n] = acc (tests)
 };
 
+// Tensor maps of one GEMM launch: A and B operands; c = the staged output
+// (16-bit [rows][N], box 64x32, 128B swizzle; or the fp32 residual, box 32x32,
+// 128B swizzle); d = the 16-bit copy of the residual (box 32x32, 64B swizzle).
+struct GemmMaps {
+  CUtensorMap a, b, c, d;
+};
+
 struct GemmArgs {
   int m_rows;           // uniform: valid rows of A
-  int n_tiles;          // uniform: N / 256
+  int n_tiles;          // uniform: N / 256 (full-width tiles)
+  int gate_tile;        // uniform: 1 = one extra 16-column tile after the n_tiles (QKV gate logits)
   int k_blocks;         // K / 64
   int num_tiles;        // total tiles
   const int4* tiles;    // grouped: per-chunk tile table {a_row, b_row, n0, meta}
   int tiles_per_chunk;  // grouped: entries of the table
   int chunk_rows;       // grouped: A-row offset between chunk replicas
   int b_box16;          // 1: B loaded as n_size/16 boxes of 16 rows
-  int a_strided;        // 1: A is a 3-D map (K, a_d1, a_d2) and a tile is 128 rows
-                        //    (g0 + r) * a_d1 + t at one t (uniform mode only)
-  int a_d1, a_d2;
-  void* out;
+  void* out;            // direct epilogues
   long long ldo;
   const float* bias;
-  float* resid;
-  long long ldr;
+  const float* row_inv;  // per-row RMSNorm factor applied to the accumulator (null = 1)
+  float* row_inv_out;    // kEpiResidual: per-row factor of the updated residual
   const float2* rope;   // [positions][32] (cos, sin)
   int pos_div;
   int pos_mod;
   int rope_cols;
+  const float* gate_b;  // QKV gate tile: [8]
+  float* gates_out;     // QKV gate tile: [rows][8]
   int frames;           // mask: frames per chunk (T)
   int mask_ref_layout;  // mask: 1 = reference [1025][2][T][2], 0 = frame-major [C][T][1025][2][2]
   int* err;
@@ -66,17 +73,18 @@ inline int4 make_tile(int a_row, int b_row, int n0, int m_valid, int n_size, int
   return make_int4(a_row, b_row, n0, m_valid | (n_size << 8) | (band << 17));
 }
 
+// 2-D map over a row-major [outer][inner] matrix of 16-bit (bf16 or f16) or
+// fp32 (elem_bytes 4) elements; swizzle_bytes 0, 64 or 128.
 bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t outer,
-                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle_bytes,
                   bool bf16);
-bool make_tmap_3d_rows(CUtensorMap* map, const void* base, uint64_t k, uint64_t d1, uint64_t d2, bool bf16);
 bool make_tmap_4d(CUtensorMap* map, const void* base, int elem_bytes, const uint64_t dims[4],
                   const uint64_t strides_bytes[3], const uint32_t box[4], bool bf16);
 
 // Launches the persistent tcgen05 GEMM  C = A[M][K] * B[N][K]^T  with the given
 // epilogue.  A and B are 16-bit (f16 or bf16 per `bf16`).
-cudaError_t launch_gemm(int epilogue, bool bf16, const CUtensorMap& map_a, const CUtensorMap& map_b,
-                        const GemmArgs& args, int sm_count, cudaStream_t stream);
+cudaError_t launch_gemm(int epilogue, bool bf16, const GemmMaps& maps, const GemmArgs& args, int sm_count,
+                        cudaStream_t stream);
 
 // ------------------------------------------------------------------ attention
 struct AttnArgs {
@@ -118,9 +126,11 @@ cudaError_t launch_band_split(const float* spec, int segments, int frames, const
                               const long long* band_wt_offset, const float* band_gamma,
                               const int* band_gamma_offset, const float* band_bias, float* x,
                               cudaStream_t stream);
-cudaError_t launch_norm(const float* x, long long rows, const float* gamma, const float* gate_w,
-                        const float* gate_b, void* normed, float* gates, bool bf16, int remap_s0,
-                        int remap_l0, cudaStream_t stream);
+// Row statistics of the fp32 residual: x16 = 16-bit copy of x and
+// inv = sqrt(256) / sqrt(sum x^2 + 1e-12) per row.  With remap_s0 > 0 the rows
+// of a physical [remap_s0][remap_l0] token grid are written as [l0][s0].
+cudaError_t launch_row_stats(const float* x, long long rows, void* x16, float* inv, bool bf16, int remap_s0,
+                             int remap_l0, cudaStream_t stream);
 cudaError_t launch_istft_frames(const float* spec, const float* mask, int segments, int frames,
                                 const float* window, const float2* twiddle, float* frames_out,
                                 cudaStream_t stream);
