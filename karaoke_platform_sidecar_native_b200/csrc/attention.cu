@@ -372,11 +372,13 @@ cudaError_t launch_typed(const CUtensorMap& map, const AttnArgs& args, cudaStrea
 constexpr int kPairThreads = 320;
 constexpr float kRescaleLog2 = 8.0f;
 
+constexpr int kKvStages = 3;   // K/V ring depth: loads run two tiles ahead of the PV that frees a stage
+
 struct PairSmem {
   static constexpr int kQ = 0;                       // 2 x 16 KB
-  static constexpr int kK = kQ + 2 * kQBytes;        // 2 stages x 16 KB
-  static constexpr int kV = kK + 2 * kQBytes;        // 2 stages x 16 KB
-  static constexpr int kP = kV + 2 * kQBytes;        // 2 tiles x 32 KB
+  static constexpr int kK = kQ + 2 * kQBytes;        // kKvStages x 16 KB
+  static constexpr int kV = kK + kKvStages * kQBytes;  // kKvStages x 16 KB
+  static constexpr int kP = kV + kKvStages * kQBytes;  // 2 tiles x 32 KB
   static constexpr int kBar = kP + 2 * kPBytes;
   static constexpr int kBytes = 1024 + kBar + 256;
 };
@@ -393,14 +395,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint8_t* sP = smem + L::kP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;     // [tile]
-  uint64_t* s_empty = bars + 7;    // [tile]
-  uint64_t* p_full = bars + 9;     // [tile]
-  uint64_t* o_full = bars + 11;    // [tile]
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* kv_full = bars + 1;                 // [kKvStages]
+  uint64_t* kv_empty = kv_full + kKvStages;     // [kKvStages]
+  uint64_t* s_full = kv_empty + kKvStages;      // [tile]
+  uint64_t* s_empty = s_full + 2;               // [tile]
+  uint64_t* p_full = s_empty + 2;               // [tile]
+  uint64_t* o_full = p_full + 2;                // [tile]
+  uint64_t* drain = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -426,9 +428,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKvStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
@@ -461,8 +465,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       load_tile(sQ, q_full, head * kDimHead, q0);
       if (ntiles == 2) load_tile(sQ + kQBytes, q_full, head * kDimHead, q0 + kTile);
       for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        const uint32_t par = static_cast<uint32_t>(j >> 1) & 1u;
+        const int st = j % kKvStages;
+        const uint32_t par = static_cast<uint32_t>(j / kKvStages) & 1u;
         if (!mbar_wait(&kv_empty[st], par ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kQBytes);
         load_tile(sK + st * kQBytes, &kv_full[st], kDimInner + head * kDimHead, j * kTile);
@@ -473,7 +477,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (lane == 0) {
       const uint32_t bf = ElemTraits<T>::kBf16;
       auto issue_pv = [&](int i) -> bool {
-        const int st = i & 1;
+        const int st = i % kKvStages;
         const int nc = min(kTile, round16(length - i * kTile));
         const uint32_t idesc = idesc_f16(kTile, kDimHead, bf, 0, 1);
         const uint32_t v_addr = smem_u32(sV + st * kQBytes);
@@ -493,8 +497,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, args.err, kErrWaitMma);
       for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, args.err, kErrWaitMma)) {
+        const int st = j % kKvStages;
+        if (!mbar_wait(&kv_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, args.err, kErrWaitMma)) {
           ok = false;
           break;
         }
@@ -542,57 +546,71 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tc_fence_after();
       const int valid = length - j * kTile;
       const int nc = min(kTile, round16(valid));
-      // All 128 S columns are read; columns >= valid (stale or never written
-      // by a narrower MMA) are masked below.
-      uint32_t ra[32], rb[32], rc[32], rd[32];
-      tmem_ld32(s_addr + 0, ra);
-      tmem_ld32(s_addr + 32, rb);
-      tmem_ld32(s_addr + 64, rc);
-      tmem_ld32(s_addr + 96, rd);
-      tmem_wait_ld();
-      reg_fence(ra);
-      reg_fence(rb);
-      reg_fence(rc);
-      reg_fence(rd);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[x]);
-      float v[kTile];
+      // The tile is processed as two 64-column halves.  The reference maximum
+      // only has to keep exp2 below 2^8, so each half is exponentiated against
+      // the current reference; when the second half raises it, the packed P of
+      // the first half is rescaled.  All 128 S columns are read; columns >=
+      // valid (stale, or never written by a narrower MMA) are masked.
+      uint32_t pk[kTile / 2];   // P packed to 16-bit pairs
+      float sum = 0.f;
+      float factor = 1.0f;      // accumulated rescale of O and l for this tile
+      bool raised = false;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        v[q] = __uint_as_float(ra[q]);
-        v[32 + q] = __uint_as_float(rb[q]);
-        v[64 + q] = __uint_as_float(rc[q]);
-        v[96 + q] = __uint_as_float(rd[q]);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(s_addr + 64 * hh, ra);
+        tmem_ld32(s_addr + 64 * hh + 32, rb);
+        tmem_wait_ld();
+        reg_fence(ra);
+        reg_fence(rb);
+        if (hh == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_empty[x]);   // S buffer free for the next tile
+        }
+        float v[64];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          v[q] = __uint_as_float(ra[q]);
+          v[32 + q] = __uint_as_float(rb[q]);
+        }
+        if (valid < kTile) {   // only the last KV tile has keys past the end
+#pragma unroll
+          for (int q = 0; q < 64; ++q)
+            if (64 * hh + q >= valid) v[q] = -INFINITY;
+        }
+        float mxs[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mxs[a] = v[a];
+#pragma unroll
+        for (int q = 8; q < 64; ++q) mxs[q & 7] = fmaxf(mxs[q & 7], v[q]);
+        const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                               fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        // Raise the reference maximum only when this half would exceed 2^8.
+        if ((mx - m_ref) * kScaleLog2 > kRescaleLog2) {
+          const float f = ex2_approx((m_ref - mx) * kScaleLog2);   // 0 when m_ref = -inf
+          m_ref = mx;
+          factor *= f;
+          sum *= f;
+          raised = true;
+          if (hh == 1) {
+            const uint32_t f2 = ElemTraits<T>::pack2(f, f);
+#pragma unroll
+            for (int q = 0; q < 32; ++q) pk[q] = ElemTraits<T>::mul2(pk[q], f2);
+          }
+        }
+        const float mscaled = m_ref * kScaleLog2;
+        float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < 64; q += 2) {
+          const float p0 = ex2_approx(fmaf(v[q], kScaleLog2, -mscaled));
+          const float p1 = ex2_approx(fmaf(v[q + 1], kScaleLog2, -mscaled));
+          sums[(q >> 1) & 7] += p0 + p1;
+          pk[32 * hh + q / 2] = ElemTraits<T>::pack2(p0, p1);
+        }
+        sum += ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
       }
-      if (valid < kTile) {   // only the last KV tile has keys past the end
-#pragma unroll
-        for (int q = 0; q < kTile; ++q)
-          if (q >= valid) v[q] = -INFINITY;
-      }
-      // Row maximum as a tree over 8 independent accumulators.
-      float mxs[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) mxs[a] = v[a];
-#pragma unroll
-      for (int q = 8; q < kTile; ++q) mxs[q & 7] = fmaxf(mxs[q & 7], v[q]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
-      // Raise the reference maximum only when this tile would exceed 2^8.
-      const bool raise = (mx - m_ref) * kScaleLog2 > kRescaleLog2;
-      const float m_new = raise ? mx : m_ref;
-      const float factor = raise ? ex2_approx((m_ref - m_new) * kScaleLog2) : 1.0f;   // 0 when m_ref = -inf
-      const float mscaled = m_new * kScaleLog2;
-      float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[kTile / 2];   // P packed to 16-bit pairs, freeing the fp32 scores
-#pragma unroll
-      for (int q = 0; q < kTile; q += 2) {
-        const float p0 = ex2_approx(fmaf(v[q], kScaleLog2, -mscaled));
-        const float p1 = ex2_approx(fmaf(v[q + 1], kScaleLog2, -mscaled));
-        sums[(q >> 1) & 7] += p0 + p1;
-        pk[q / 2] = ElemTraits<T>::pack2(p0, p1);
-      }
-      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+      const bool raise = raised;
       if (j > 0) {
         // PV of the previous tile must be complete before P is overwritten and
         // before this row of O is rescaled.
@@ -616,7 +634,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
       }
       l_run = l_run * factor + sum;
-      m_ref = m_new;
 #pragma unroll
       for (int g = 0; g < kTile / 8; ++g) {
         if (g * 8 < nc) {
