@@ -39,7 +39,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=default", "-I", os.path.join(ROOT, "include"),
-           "-I", os.path.join(HERE, "csrc"), "--expt-relaxed-constexpr", "-o", LIB + ".tmp", *sources()]
+           "-I", os.path.join(HERE, "csrc"), "--expt-relaxed-constexpr",
+           # -z defs: an unresolved symbol fails the link instead of the first dlopen.
+           "-Xlinker", "-z,defs", "-o", LIB + ".tmp", *sources()]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))

@@ -553,7 +553,7 @@ bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan&
   at.gates = g->gates;
   at.out = g->attn;
   at.err = g->d_err;
-  if (!launched(g, launch_attention(bf, q4, at, g->stream), ax.length <= 128 ? "attention (L<=128)" : "attention (L>128)"))
+  if (!launched(g, launch_attention(bf, q4, at, g->sm_count, g->stream), ax.length <= 128 ? "attention (L<=128)" : "attention (L>128)"))
     return false;
 
   // x += out(attn); x16 and row_inv of the new x
@@ -1255,7 +1255,7 @@ int vocalarc_b200_stage_attention(native_gpu* g, const void* qkv, const float* g
   at.gates = gates;
   at.out = out;
   at.err = g->d_err;
-  return launched(g, launch_attention(g->bf16 != 0, q4, at, g->stream), "stage attention") ? 1 : 0;
+  return launched(g, launch_attention(g->bf16 != 0, q4, at, g->sm_count, g->stream), "stage attention") ? 1 : 0;
 }
 
 int vocalarc_b200_stage_stft(native_gpu* g, const float* audio, int segments, int length, float* spec) {

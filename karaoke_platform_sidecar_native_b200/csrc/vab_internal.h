@@ -97,7 +97,7 @@ struct AttnArgs {
   void* out;           // [rows][512] gated attention output (16-bit)
   int* err;
 };
-cudaError_t launch_attention(bool bf16, const CUtensorMap& map_qkv, const AttnArgs& args,
+cudaError_t launch_attention(bool bf16, const CUtensorMap& map_qkv, const AttnArgs& args, int sm_count,
                              cudaStream_t stream);
 
 // ------------------------------------------------------------------ elementwise / spectral
