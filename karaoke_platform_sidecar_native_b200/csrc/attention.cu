@@ -39,27 +39,69 @@ __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity, int* 
   return true;
 }
 
+
+// 2^x on the FMA pipe for a pair of values, x <= 8 (x < -125 is clamped; the
+// result is then below 2^-124 and rounds to zero in 16 bits).  x = j + f with
+// j = rint(x) from the 1.5 * 2^23 addition, f in [-1/2, 1/2]; 2^f from a
+// degree-3 polynomial (coefficients fitted here for minimum relative error on
+// [-1/2, 1/2], max relative error 7.5e-5, below 16-bit rounding); 2^j is added
+// to the exponent field.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.0f;
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kMagic, kMagic));
+  const float2 j = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(f, make_float2(0.05517097935080528f, 0.05517097935080528f),
+                        make_float2(0.24260970950126648f, 0.24260970950126648f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = __ffma2_rn(p, f, make_float2(0.9999281764030457f, 0.9999281764030457f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Of every 8 exponent pairs, this many go to the FMA-pipe polynomial and the
+// rest to MUFU ex2 (16 results per clock per SM), balancing the two pipes;
+// 2 of 8 measured fastest against 0, 3 and 4.
+constexpr int kPolyPairs = 2;
+
 // ---------------------------------------------------------------------------
 // Long sequences (L > 128): one CTA computes two 128-query tiles (A, B) of one
 // (sequence, head) that share every K/V tile.  Warps 2-5 own tile A, warps 6-9
-// tile B (one query row per thread).  O accumulates in TMEM across KV tiles;
-// a row's reference maximum m is raised only when a tile's maximum exceeds it
-// by more than 2^8 in exp2 units, in which case that row of O (TMEM) and its
-// running sum are rescaled -- otherwise P = exp2((s - m) c) <= 256 stays exact
-// enough in 16 bits and no O traffic is needed.
+// tile B (one query row per thread).  P goes to tensor memory and the PV MMA
+// reads it from there (A operand in TMEM), so P never touches shared memory.
+// O accumulates in TMEM across KV tiles; a row's reference maximum m is raised
+// only when a tile's maximum exceeds it by more than 2^8 in exp2 units, in
+// which case that row of O (TMEM) and its running sum are rescaled --
+// otherwise P = exp2((s - m) c) <= 256 stays exact enough in 16 bits and no O
+// traffic is needed.
+//
+// The MMA warp runs its loop warp-uniform and issues each MMA under
+// elect.sync, with descriptors advanced by constant offsets: a tcgen05.mma is
+// then issued in a few cycles, well under its 32-64 cycle execution time.
 constexpr int kPairThreads = 320;
 constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int kKvStages = 3;   // K/V ring depth: loads run two tiles ahead of the PV that frees a stage
 
 struct PairSmem {
-  static constexpr int kQ = 0;                       // 2 x 16 KB
-  static constexpr int kK = kQ + 2 * kQBytes;        // kKvStages x 16 KB
+  static constexpr int kQ = 0;                         // 2 x 16 KB
+  static constexpr int kK = kQ + 2 * kQBytes;          // kKvStages x 16 KB
   static constexpr int kV = kK + kKvStages * kQBytes;  // kKvStages x 16 KB
-  static constexpr int kP = kV + kKvStages * kQBytes;  // 2 tiles x 32 KB
-  static constexpr int kBar = kP + 2 * kPBytes;
+  static constexpr int kBar = kV + kKvStages * kQBytes;
   static constexpr int kBytes = 1024 + kBar + 256;
 };
+
+// TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384),
+// P_A [384,448), P_B [448,512) (P: two 16-bit values per column).
+constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
 
 template <typename T>
 __global__ void __launch_bounds__(kPairThreads, 1)
@@ -70,7 +112,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint8_t* sQ = smem + L::kQ;
   uint8_t* sK = smem + L::kK;
   uint8_t* sV = smem + L::kV;
-  uint8_t* sP = smem + L::kP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                 // [kKvStages]
@@ -128,7 +169,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384).
 
   if (warp == 0) {
     if (lane == 0) {
@@ -152,55 +192,64 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t bf = ElemTraits<T>::kBf16;
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % kKvStages;
-        const int nc = min(kTile, round16(length - i * kTile));
-        const uint32_t idesc = idesc_f16(kTile, kDimHead, bf, 0, 1);
-        const uint32_t v_addr = smem_u32(sV + st * kQBytes);
-        for (int x = 0; x < ntiles; ++x) {
-          if (!mbar_wait(&p_full[x], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitMma)) return false;
-          tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP + x * kPBytes);
-          for (int kk = 0; kk < nc / 16; ++kk) {
-            const uint64_t da = sw128_desc(p_addr + (kk >> 2) * (kTile * 128) + (kk & 3) * 32, 16, 1024);
-            const uint64_t db = sw128_desc(v_addr + kk * 2048, 8192, 1024);
-            umma_f16(tmem_base + 256 + x * kDimHead, da, db, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-          }
+    // MMA warp: warp-uniform control flow, one elected lane issues.
+    const uint32_t bf = ElemTraits<T>::kBf16;
+    const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
+    const uint64_t q_desc = sw128_desc(smem_u32(sQ), 16, 1024);
+    const uint64_t k_desc = sw128_desc(smem_u32(sK), 16, 1024);
+    const uint64_t v_desc = sw128_desc(smem_u32(sV), 8192, 1024);
+    auto issue_pv = [&](int i) -> bool {
+      const int st = i % kKvStages;
+      const int ksteps = min(kTile, round16(length - i * kTile)) / 16;
+      const uint64_t vd = v_desc + static_cast<uint64_t>((st * kQBytes) >> 4);
+      for (int x = 0; x < ntiles; ++x) {
+        if (!mbar_wait_warp(&p_full[x], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitMma))
+          return false;
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t o_col = tmem_base + kColO + x * kDimHead;
+          const uint32_t p_col = tmem_base + kColP + x * (kTile / 2);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            if (kk < ksteps) umma_f16_ts(o_col, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&o_full[x]);
         }
-        umma_commit(&kv_empty[st]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag, args.err, kErrWaitMma);
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % kKvStages;
-        if (!mbar_wait(&kv_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, args.err, kErrWaitMma)) {
+        __syncwarp();
+      }
+      if (elect_one()) umma_commit(&kv_empty[st]);
+      __syncwarp();
+      return true;
+    };
+    bool ok = mbar_wait_warp(q_full, 0, abort_flag, args.err, kErrWaitMma);
+    for (int j = 0; ok && j < nkv; ++j) {
+      const int st = j % kKvStages;
+      if (!mbar_wait_warp(&kv_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, args.err,
+                          kErrWaitMma)) {
+        ok = false;
+        break;
+      }
+      const int nc = min(kTile, round16(length - j * kTile));
+      const uint32_t idesc_s = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
+      const uint64_t kd = k_desc + static_cast<uint64_t>((st * kQBytes) >> 4);
+      for (int x = 0; x < ntiles && ok; ++x) {
+        if (!mbar_wait_warp(&s_empty[x], (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag, args.err, kErrWaitMma)) {
           ok = false;
           break;
         }
-        const int nc = min(kTile, round16(length - j * kTile));
-        const uint32_t idesc = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
-        const uint32_t k_addr = smem_u32(sK + st * kQBytes);
-        for (int x = 0; x < ntiles && ok; ++x) {
-          if (!mbar_wait(&s_empty[x], (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag, args.err, kErrWaitMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t q_addr = smem_u32(sQ + x * kQBytes);
+        tc_fence_after();
+        if (elect_one()) {
+          const uint64_t qd = q_desc + static_cast<uint64_t>((x * kQBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kDimHead / 16; ++kk) {
-            const uint64_t da = sw128_desc(q_addr + kk * 32, 16, 1024);
-            const uint64_t db = sw128_desc(k_addr + kk * 32, 16, 1024);
-            umma_f16(tmem_base + x * kTile, da, db, idesc, kk != 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kDimHead / 16; ++kk)
+            umma_f16(tmem_base + kColS + x * kTile, qd + 2 * kk, kd + 2 * kk, idesc_s, kk != 0 ? 1u : 0u);
           umma_commit(&s_full[x]);
         }
-        if (ok && j > 0 && !issue_pv(j - 1)) ok = false;
+        __syncwarp();
       }
-      if (ok) issue_pv(nkv - 1);
+      if (ok && j > 0 && !issue_pv(j - 1)) ok = false;
+    }
+    if (ok) issue_pv(nkv - 1);
+    if (elect_one()) {
       umma_commit(drain);
       wait_drain(drain, 0, args.err);
     }
@@ -210,9 +259,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem_base + x * kTile + lane_off;
-    const uint32_t o_addr = tmem_base + 256 + x * kDimHead + lane_off;
-    uint8_t* p_base = sP + x * kPBytes + (row >> 3) * 1024 + (row & 7) * 128;
+    const uint32_t s_addr = tmem_base + kColS + x * kTile + lane_off;
+    const uint32_t o_addr = tmem_base + kColO + x * kDimHead + lane_off;
+    const uint32_t p_addr = tmem_base + kColP + x * (kTile / 2) + lane_off;
     bool ok = x < ntiles;
     float m_ref = -INFINITY;   // reference maximum (raw score units)
     float l_run = 0.f;
@@ -223,7 +272,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
       tc_fence_after();
       const int valid = length - j * kTile;
-      const int nc = min(kTile, round16(valid));
       // The tile is processed as two 64-column halves.  The reference maximum
       // only has to keep exp2 below 2^8, so each half is exponentiated against
       // the current reference; when the second half raises it, the packed P of
@@ -261,9 +309,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int a = 0; a < 8; ++a) mxs[a] = v[a];
 #pragma unroll
-        for (int q = 8; q < 64; ++q) mxs[q & 7] = fmaxf(mxs[q & 7], v[q]);
-        const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                               fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        for (int q = 8; q < 64; q += 16)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) mxs[a] = fmax3(mxs[a], v[q + a], v[q + 8 + a]);
+        const float mx = fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
         // Raise the reference maximum only when this half would exceed 2^8.
         if ((mx - m_ref) * kScaleLog2 > kRescaleLog2) {
           const float f = ex2_approx((m_ref - mx) * kScaleLog2);   // 0 when m_ref = -inf
@@ -278,15 +327,25 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
         }
         const float mscaled = m_ref * kScaleLog2;
-        float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
+        const float2 nm2 = make_float2(-mscaled, -mscaled);
+        float2 sums[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                          make_float2(0.f, 0.f)};
 #pragma unroll
         for (int q = 0; q < 64; q += 2) {
-          const float p0 = ex2_approx(fmaf(v[q], kScaleLog2, -mscaled));
-          const float p1 = ex2_approx(fmaf(v[q + 1], kScaleLog2, -mscaled));
-          sums[(q >> 1) & 7] += p0 + p1;
-          pk[32 * hh + q / 2] = ElemTraits<T>::pack2(p0, p1);
+          const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
+          float2 p2;
+          if (((q >> 1) & 7) < kPolyPairs) {
+            p2 = exp2_poly2(x2);
+          } else {
+            p2.x = ex2_approx(x2.x);
+            p2.y = ex2_approx(x2.y);
+          }
+          sums[(q >> 1) & 3] = __fadd2_rn(sums[(q >> 1) & 3], p2);
+          pk[32 * hh + q / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
         }
-        sum += ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+        const float2 s01 = __fadd2_rn(__fadd2_rn(sums[0], sums[1]), __fadd2_rn(sums[2], sums[3]));
+        sum += s01.x + s01.y;
       }
       const bool raise = raised;
       if (j > 0) {
@@ -308,20 +367,20 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             for (int d = 0; d < 32; ++d) r[d] = __float_as_uint(__uint_as_float(r[d]) * factor);
             tmem_st32(o_addr + half * 32, r);
           }
-          tmem_wait_st();
         }
       }
       l_run = l_run * factor + sum;
+      {
+        uint32_t p0[32], p1[32];
 #pragma unroll
-      for (int g = 0; g < kTile / 8; ++g) {
-        if (g * 8 < nc) {
-          const int atom = g >> 3;
-          const int chunk16 = g & 7;
-          *reinterpret_cast<uint4*>(p_base + atom * (kTile * 128) + ((chunk16 ^ (row & 7)) << 4)) =
-              make_uint4(pk[g * 4 + 0], pk[g * 4 + 1], pk[g * 4 + 2], pk[g * 4 + 3]);
+        for (int q = 0; q < 32; ++q) {
+          p0[q] = pk[q];
+          p1[q] = pk[32 + q];
         }
+        tmem_st32(p_addr, p0);
+        tmem_st32(p_addr + 32, p1);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[x]);
