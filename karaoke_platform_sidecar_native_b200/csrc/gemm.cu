@@ -77,7 +77,29 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmArgs& args, int tile) 
   return t;
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865475f)); }
+// Exact-erf GELU, x * h(x) with h = (1 + erf(x / sqrt 2)) / 2, for a pair of
+// values on the FMA pipe (no MUFU).  w = clamp(x k + 1/2, 0, 1) - 1/2 maps
+// x in [-c sqrt 2, c sqrt 2] (c = 3.1) onto [-1/2, 1/2]; h = 1/2 + w P(w^2)
+// with P of degree 9, least-squares fitted here (Lawson-weighted towards
+// minimax) to erf(2 c w) / 2.  |h error| <= 1.3e-5 everywhere (erfc(3.1) / 2 =
+// 5.8e-6 beyond the clamp), so |gelu error| <= 1.5e-5 for |x| < 4 -- far
+// below the 16-bit rounding of the stored result.
+__device__ __forceinline__ float2 gelu_pair(float2 x) {
+  constexpr float k = 0.11404947936534882f;
+  float2 w;
+  w.x = __saturatef(fmaf(x.x, k, 0.5f));
+  w.y = __saturatef(fmaf(x.y, k, 0.5f));
+  w = __fadd2_rn(w, make_float2(-0.5f, -0.5f));
+  const float2 w2 = __fmul2_rn(w, w);
+  constexpr float c[10] = {3.4978649616241455f,  -44.785457611083984f, 513.5380249023438f, -4584.1708984375f,
+                           31743.6796875f,       -166752.21875f,       634539.25f,         -1627862.625f,
+                           2492293.25f,          -1707633.25f};
+  float2 p = make_float2(c[9], c[9]);
+#pragma unroll
+  for (int i = 8; i >= 0; --i) p = __ffma2_rn(p, w2, make_float2(c[i], c[i]));
+  const float2 h = __ffma2_rn(w, p, make_float2(0.5f, 0.5f));
+  return __fmul2_rn(x, h);
+}
 
 __device__ __forceinline__ float sigmoidf(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
@@ -152,21 +174,32 @@ __device__ __forceinline__ void epilogue_out16(const GemmArgs& args, const CUten
       tmem_wait_ld();
       reg_fence(r);
       float v[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * inv;
       if (EPI == kEpiGelu || (EPI == kEpiStore && args.bias != nullptr)) {
+        // v = acc * inv + bias, two columns per instruction.
+        const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 b = __ldg(reinterpret_cast<const float4*>(args.bias + n + 32 * hh) + q);
-          v[4 * q] += b.x;
-          v[4 * q + 1] += b.y;
-          v[4 * q + 2] += b.z;
-          v[4 * q + 3] += b.w;
+          const float2 lo = __ffma2_rn(make_float2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])), inv2,
+                                       make_float2(b.x, b.y));
+          const float2 hi = __ffma2_rn(make_float2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])),
+                                       inv2, make_float2(b.z, b.w));
+          v[4 * q] = lo.x;
+          v[4 * q + 1] = lo.y;
+          v[4 * q + 2] = hi.x;
+          v[4 * q + 3] = hi.y;
         }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * inv;
       }
       if (EPI == kEpiGelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        for (int j = 0; j < 32; j += 2) {
+          const float2 g = gelu_pair(make_float2(v[j], v[j + 1]));
+          v[j] = g.x;
+          v[j + 1] = g.y;
+        }
       }
       if (do_rope) {
         // A 64-column step is one head: pairs (2i, 2i+1) rotate by rope pair i.
@@ -490,45 +523,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
-      const uint32_t idesc_base = idesc_f16(kBM, 0, ElemTraits<T>::kBf16, 0, 0);
-      int stage = 0;
-      uint32_t phase = 0;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < args.num_tiles && !*abort_flag; tile += gridDim.x, ++it) {
-        const TileInfo ti = decode_tile(args, tile);
-        const int acc = it & 1;
-        const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.err, kErrWaitMma)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
-        const uint32_t idesc = idesc_base | ((static_cast<uint32_t>(ti.n_size) >> 3) << 17);
-        bool ok = true;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, args.err, kErrWaitMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * kABytes);
-          const uint32_t b_base = smem_u32(sB + stage * kBBytes);
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t da = sw128_desc(a_base + kk * 32, 16, 1024);
-            const uint64_t db = sw128_desc(b_base + kk * 32, 16, 1024);
-            umma_f16(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
-          }
-          umma_commit(&empty[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+    // ---------------- MMA issuer: warp-uniform loop, one elected lane issues;
+    // descriptors advance by constant offsets (K step of 16 = 32 bytes).
+    const uint32_t idesc_base = idesc_f16(kBM, 0, ElemTraits<T>::kBf16, 0, 0);
+    const uint64_t a_desc0 = sw128_desc(smem_u32(sA), 16, 1024);
+    const uint64_t b_desc0 = sw128_desc(smem_u32(sB), 16, 1024);
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++it) {
+      const TileInfo ti = decode_tile(args, tile);
+      const int acc = it & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
+      if (!mbar_wait_warp(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.err, kErrWaitMma)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+      const uint32_t idesc = idesc_base | ((static_cast<uint32_t>(ti.n_size) >> 3) << 17);
+      bool ok = true;
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (!mbar_wait_warp(&full[stage], phase, abort_flag, args.err, kErrWaitMma)) {
+          ok = false;
+          break;
         }
-        if (!ok) break;
-        umma_commit(&acc_full[acc]);
+        tc_fence_after();
+        if (elect_one()) {
+          const uint64_t da = a_desc0 + static_cast<uint64_t>((stage * kABytes) >> 4);
+          const uint64_t db = b_desc0 + static_cast<uint64_t>((stage * kBBytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) umma_f16(d_tmem, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
-      // Drain: every MMA issued above has completed before TMEM is released.
+      if (!ok) break;
+      if (elect_one()) umma_commit(&acc_full[acc]);
+      __syncwarp();
+    }
+    // Drain: every MMA issued above has completed before TMEM is released.
+    if (elect_one()) {
       umma_commit(drain);
       wait_no_abort_check(drain, 0, args.err);
     }
