@@ -450,34 +450,52 @@ cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, cudaStream
 
 // ---------------------------------------------------------------------------
 // Short sequences (L <= 128, the band axis: L = 90): a persistent CTA walks
-// (sequence, head) items; consecutive items alternate between two slots, each
-// with its own Q, K, V and P buffers, TMEM S and O columns and softmax warps
-// (warps 2-5: slot 0, warps 6-9: slot 1), so the TMA loads of one item overlap
-// the MMA and softmax of the other.  One KV tile per item: plain softmax.
+// (sequence, head) items.  The kernel moves about 46 KB per item (q, k, v in,
+// gated output out), so the design keeps loads in flight and every stage busy:
+// four shared-memory stages of Q, K, V run ahead of the MMAs; items alternate
+// between two softmax warp groups (warps 2-5: group 0, warps 6-9: group 1),
+// each with one TMEM S buffer (P written over it) and two O buffers, and a
+// group writes an item's output only after the softmax of its next item, so
+// the PV MMA's latency is hidden.  One KV tile per item: plain softmax.  A
+// warp whose 32 rows all lie at or past the sequence length (rows 96-127 for
+// L = 90) does no softmax or output work: the rows of P it leaves stale only
+// reach rows of O that are never stored.
 constexpr int kItemThreads = 320;
+constexpr int kItemStages = 4;
 
 struct ItemSmem {
-  static constexpr int kSlot = 3 * kQBytes + kPBytes;   // Q, K, V, P: 80 KB
-  static constexpr int kBar = 2 * kSlot;
+  static constexpr int kStage = 3 * kQBytes;   // Q, K, V: 48 KB
+  static constexpr int kBar = kItemStages * kStage;
   static constexpr int kBytes = 1024 + kBar + 256;
 };
+
+// Output row of query position `pos` of sequence `seq` (32-bit: rows < 2^31).
+__device__ __forceinline__ int attn_row(const AttnArgs& args, int seq, int pos) {
+  if (args.pos_dim == 1) return seq * args.d1 + pos;
+  const int c_a = seq % args.d1;
+  const int c_b = seq / args.d1;
+  return (c_b * args.d2 + pos) * args.d1 + c_a;
+}
 
 template <typename T, int NCOLS>
 __global__ void __launch_bounds__(kItemThreads, 1)
     attention_items_kernel(const __grid_constant__ CUtensorMap map, const AttnArgs args) {
   static_assert(NCOLS % 32 == 0 && NCOLS <= kTile, "score columns per row");
   using L = ItemSmem;
+  // TMEM columns: S/P of group g at [g * NCOLS, +NCOLS); O buffer b of group g
+  // at [2 * NCOLS + 64 (2 g + b), +64).
+  constexpr uint32_t kColO = 2 * NCOLS;
+  static_assert(2 * NCOLS + 4 * kDimHead <= 512, "TMEM columns");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* full = bars;            // [slot]
-  uint64_t* slot_free = bars + 2;   // [slot]
-  uint64_t* s_full = bars + 4;
-  uint64_t* s_empty = bars + 6;
-  uint64_t* p_full = bars + 8;
-  uint64_t* o_full = bars + 10;
-  uint64_t* o_empty = bars + 12;
-  uint64_t* drain = bars + 14;
+  uint64_t* full = bars;                             // [stage]
+  uint64_t* stage_free = bars + kItemStages;         // [stage]
+  uint64_t* s_full = bars + 2 * kItemStages;         // [group]
+  uint64_t* p_full = s_full + 2;                     // [group]
+  uint64_t* o_full = p_full + 2;                     // [group][buffer]
+  uint64_t* o_free = o_full + 4;                     // [group][buffer]
+  uint64_t* drain = o_free + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -485,18 +503,21 @@ __global__ void __launch_bounds__(kItemThreads, 1)
   const int lane = lane_id();
   const int length = args.length;
   const int nc = round16(length);
-  const long long total = static_cast<long long>(args.sequences) * kHeads;
-  const int n_local = blockIdx.x < total ? static_cast<int>((total - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  const int total = args.sequences * kHeads;   // host checks < 2^31
+  const int n_local = static_cast<int>(blockIdx.x) < total ? (total - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1 : 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kItemStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&slot_free[i], 1);
+      mbar_init(&stage_free[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
+      mbar_init(&o_free[i], 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -509,195 +530,268 @@ __global__ void __launch_bounds__(kItemThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;   // S_x at 128 x, O_x at 256 + 64 x
-
-  auto item_coords = [&](int k, int& head, long long& seq, int& c_a, int& c_b) {
-    const long long item = blockIdx.x + static_cast<long long>(k) * gridDim.x;
-    head = static_cast<int>(item % kHeads);
-    seq = item / kHeads;
-    if (args.pos_dim == 1) {
-      c_a = static_cast<int>(seq % args.d2);
-      c_b = static_cast<int>(seq / args.d2);
-    } else {
-      c_a = static_cast<int>(seq % args.d1);
-      c_b = static_cast<int>(seq / args.d1);
-    }
-  };
+  const uint32_t tmem_base = *tmem_slot;
+  // Item k of this CTA: global item blockIdx.x + k * gridDim.x; head fastest.
+  auto item_of = [&](int k) { return static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x); };
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch(&map);
       for (int k = 0; k < n_local; ++k) {
-        const int x = k & 1;
-        const uint32_t par = static_cast<uint32_t>(k >> 1) & 1u;
-        if (!mbar_wait(&slot_free[x], par ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
-        int head, c_a, c_b;
-        long long seq;
-        item_coords(k, head, seq, c_a, c_b);
-        uint8_t* slot = smem + x * L::kSlot;
-        mbar_arrive_expect_tx(&full[x], 3 * kQBytes);
+        const int st = k % kItemStages;
+        const uint32_t par = static_cast<uint32_t>(k / kItemStages) & 1u;
+        if (!mbar_wait(&stage_free[st], par ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
+        const int item = item_of(k);
+        const int head = item % kHeads;
+        const int seq = item / kHeads;
+        int c_a, c_b;
+        if (args.pos_dim == 1) {
+          c_a = seq % args.d2;
+          c_b = seq / args.d2;
+        } else {
+          c_a = seq % args.d1;
+          c_b = seq / args.d1;
+        }
+        uint8_t* dst = smem + st * L::kStage;
+        mbar_arrive_expect_tx(&full[st], 3 * kQBytes);
 #pragma unroll
         for (int part = 0; part < 3; ++part) {
           const int col = part * kDimInner + head * kDimHead;
           if (args.pos_dim == 1)
-            tma_load_4d(slot + part * kQBytes, &map, &full[x], col, 0, c_a, c_b);
+            tma_load_4d(dst + part * kQBytes, &map, &full[st], col, 0, c_a, c_b);
           else
-            tma_load_4d(slot + part * kQBytes, &map, &full[x], col, c_a, 0, c_b);
+            tma_load_4d(dst + part * kQBytes, &map, &full[st], col, c_a, 0, c_b);
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t bf = ElemTraits<T>::kBf16;
-      const uint32_t idesc_s = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
-      const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
-      auto issue_pv = [&](int k) -> bool {
-        const int x = k & 1;
-        const uint32_t par = static_cast<uint32_t>(k >> 1) & 1u;
-        if (!mbar_wait(&p_full[x], par, abort_flag, args.err, kErrWaitMma)) return false;
-        if (!mbar_wait(&o_empty[x], par ^ 1u, abort_flag, args.err, kErrWaitMma)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(smem + x * L::kSlot + 3 * kQBytes);
-        const uint32_t v_addr = smem_u32(smem + x * L::kSlot + 2 * kQBytes);
-        for (int kk = 0; kk < nc / 16; ++kk) {
-          const uint64_t da = sw128_desc(p_addr + (kk >> 2) * (kTile * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t db = sw128_desc(v_addr + kk * 2048, 8192, 1024);
-          umma_f16(tmem_base + 256 + x * kDimHead, da, db, idesc_o, kk != 0 ? 1u : 0u);
-        }
-        umma_commit(&o_full[x]);
-        umma_commit(&slot_free[x]);
-        return true;
-      };
-      bool ok = true;
-      for (int k = 0; ok && k < n_local; ++k) {
-        const int x = k & 1;
-        const uint32_t par = static_cast<uint32_t>(k >> 1) & 1u;
-        if (!mbar_wait(&full[x], par, abort_flag, args.err, kErrWaitMma) ||
-            !mbar_wait(&s_empty[x], par ^ 1u, abort_flag, args.err, kErrWaitMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + x * L::kSlot);
-        const uint32_t k_addr = q_addr + kQBytes;
+    // MMA warp: warp-uniform control flow, one elected lane issues.
+    // Item k: group g = k & 1, group index i = k >> 1, O buffer b = i & 1.
+    const uint32_t bf = ElemTraits<T>::kBf16;
+    const uint32_t idesc_s = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
+    const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
+    const uint64_t base_desc_k = sw128_desc(smem_u32(smem), 16, 1024);
+    const uint64_t base_desc_v = sw128_desc(smem_u32(smem), 8192, 1024);
+    auto issue_pv = [&](int k) -> bool {
+      const int g = k & 1;
+      const int i = k >> 1;
+      const int ob = 2 * g + (i & 1);
+      const int st = k % kItemStages;
+      if (!mbar_wait_warp(&p_full[g], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitMma)) return false;
+      // O buffer ob was last used by item k - 4: its output must have been read.
+      if (i >= 2 && !mbar_wait_warp(&o_free[ob], static_cast<uint32_t>((i >> 1) - 1) & 1u, abort_flag, args.err,
+                                    kErrWaitMma))
+        return false;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint64_t vd = base_desc_v + static_cast<uint64_t>((st * L::kStage + 2 * kQBytes) >> 4);
+        const uint32_t p_col = tmem_base + g * NCOLS;
 #pragma unroll
-        for (int kk = 0; kk < kDimHead / 16; ++kk) {
-          const uint64_t da = sw128_desc(q_addr + kk * 32, 16, 1024);
-          const uint64_t db = sw128_desc(k_addr + kk * 32, 16, 1024);
-          umma_f16(tmem_base + x * kTile, da, db, idesc_s, kk != 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[x]);
-        if (k > 0 && !issue_pv(k - 1)) ok = false;
+        for (int kk = 0; kk < NCOLS / 16; ++kk)
+          if (kk * 16 < nc)
+            umma_f16_ts(tmem_base + kColO + ob * kDimHead, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
+                        kk != 0 ? 1u : 0u);
+        umma_commit(&o_full[ob]);
+        umma_commit(&stage_free[st]);
       }
-      if (ok && n_local > 0) issue_pv(n_local - 1);
+      __syncwarp();
+      return true;
+    };
+    bool ok = true;
+    for (int k = 0; ok && k < n_local; ++k) {
+      const int g = k & 1;
+      const int i = k >> 1;
+      const int st = k % kItemStages;
+      if (!mbar_wait_warp(&full[st], static_cast<uint32_t>(k / kItemStages) & 1u, abort_flag, args.err,
+                          kErrWaitMma)) {
+        ok = false;
+        break;
+      }
+      // S(k) overwrites P(k-2) of this group: PV(k-2) must have completed.
+      if (i >= 1 && !mbar_wait_warp(&o_full[2 * g + ((i - 1) & 1)], static_cast<uint32_t>((i - 1) >> 1) & 1u,
+                                    abort_flag, args.err, kErrWaitMma)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (elect_one()) {
+        const uint64_t qd = base_desc_k + static_cast<uint64_t>((st * L::kStage) >> 4);
+        const uint64_t kd = qd + static_cast<uint64_t>(kQBytes >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kDimHead / 16; ++kk)
+          umma_f16(tmem_base + g * NCOLS, qd + 2 * kk, kd + 2 * kk, idesc_s, kk != 0 ? 1u : 0u);
+        umma_commit(&s_full[g]);
+      }
+      __syncwarp();
+      if (k > 0 && !issue_pv(k - 1)) ok = false;
+    }
+    if (ok && n_local > 0) issue_pv(n_local - 1);
+    if (elect_one()) {
       umma_commit(drain);
       wait_drain(drain, 0, args.err);
     }
     __syncwarp();
   } else {
-    const int x = (warp - 2) >> 2;
+    const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
+    const bool active = quarter * 32 < length;   // warp-uniform
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem_base + x * kTile + lane_off;
-    const uint32_t o_addr = tmem_base + 256 + x * kDimHead + lane_off;
-    uint8_t* p_base = smem + x * L::kSlot + 3 * kQBytes + (row >> 3) * 1024 + (row & 7) * 128;
-    for (int k = x; k < n_local; k += 2) {
-      const uint32_t par = static_cast<uint32_t>(k >> 1) & 1u;
-      if (!mbar_wait_warp(&s_full[x], par, abort_flag, args.err, kErrWaitSoftmax)) break;
-      tc_fence_after();
-      // NCOLS >= nc score columns (32-column loads; columns >= length masked).
-      uint32_t rs[NCOLS / 32][32];
-#pragma unroll
-      for (int c = 0; c < NCOLS / 32; ++c) tmem_ld32(s_addr + 32 * c, rs[c]);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < NCOLS / 32; ++c) reg_fence(rs[c]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[x]);
-      float v[NCOLS];
-#pragma unroll
-      for (int c = 0; c < NCOLS / 32; ++c)
-#pragma unroll
-        for (int q = 0; q < 32; ++q) v[32 * c + q] = __uint_as_float(rs[c][q]);
-#pragma unroll
-      for (int q = 0; q < NCOLS; ++q)
-        if (q >= length) v[q] = -INFINITY;
-      float mxs[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) mxs[a] = v[a];
-#pragma unroll
-      for (int q = 8; q < NCOLS; ++q) mxs[q & 7] = fmaxf(mxs[q & 7], v[q]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
-      const float mscaled = mx * kScaleLog2;
-      float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[NCOLS / 2];
-#pragma unroll
-      for (int q = 0; q < NCOLS; q += 2) {
-        const float p0 = ex2_approx(fmaf(v[q], kScaleLog2, -mscaled));
-        const float p1 = ex2_approx(fmaf(v[q + 1], kScaleLog2, -mscaled));
-        sums[(q >> 1) & 7] += p0 + p1;
-        pk[q / 2] = ElemTraits<T>::pack2(p0, p1);
-      }
-      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
-      // P of item k-2 (same slot) was consumed: its O was read below before.
-#pragma unroll
-      for (int g = 0; g < NCOLS / 8; ++g) {
-        if (g * 8 < nc) {
-          const int atom = g >> 3;
-          const int chunk16 = g & 7;
-          *reinterpret_cast<uint4*>(p_base + atom * (kTile * 128) + ((chunk16 ^ (row & 7)) << 4)) =
-              make_uint4(pk[g * 4 + 0], pk[g * 4 + 1], pk[g * 4 + 2], pk[g * 4 + 3]);
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[x]);
-      if (!mbar_wait_warp(&o_full[x], par, abort_flag, args.err, kErrWaitSoftmax)) break;
+    const uint32_t s_addr = tmem_base + g * NCOLS + lane_off;
+    // Output of the previous item of this group, written after the next softmax.
+    int pend_k = -1, pend_row = 0, pend_head = 0;
+    float pend_gate = 0.f, pend_sum = 1.f;
+    auto write_output = [&]() -> bool {
+      const int i = pend_k >> 1;
+      const int ob = 2 * g + (i & 1);
+      if (!mbar_wait_warp(&o_full[ob], static_cast<uint32_t>(i >> 1) & 1u, abort_flag, args.err, kErrWaitSoftmax))
+        return false;
       tc_fence_after();
       uint32_t r0[32], r1[32];
-      tmem_ld32(o_addr, r0);
-      tmem_ld32(o_addr + 32, r1);
-      tmem_wait_ld();
-      reg_fence(r0);
-      reg_fence(r1);
+      if (active) {
+        const uint32_t o_addr = tmem_base + kColO + ob * kDimHead + lane_off;
+        tmem_ld32(o_addr, r0);
+        tmem_ld32(o_addr + 32, r1);
+        tmem_wait_ld();
+        reg_fence(r0);
+        reg_fence(r1);
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[x]);
-      if (row < length) {
-        int head, c_a, c_b;
-        long long seq;
-        item_coords(k, head, seq, c_a, c_b);
-        long long R;
-        if (args.pos_dim == 1)
-          R = seq * args.d1 + row;
-        else
-          R = (static_cast<long long>(c_b) * args.d2 + row) * args.d1 + c_a;
-        const float scale = __ldg(args.gates + R * kHeads + head) / sum;
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(args.out) + R * kDimInner + head * kDimHead);
+      if (lane == 0) mbar_arrive(&o_free[ob]);
+      if (active && row < length) {
+        const float scale = pend_gate / pend_sum;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(args.out) + static_cast<long long>(pend_row) * kDimInner +
+                                              pend_head * kDimHead);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
+        for (int gq = 0; gq < 4; ++gq) {
           uint4 w;
-          w.x = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 0]) * scale, __uint_as_float(r0[g * 8 + 1]) * scale);
-          w.y = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 2]) * scale, __uint_as_float(r0[g * 8 + 3]) * scale);
-          w.z = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 4]) * scale, __uint_as_float(r0[g * 8 + 5]) * scale);
-          w.w = ElemTraits<T>::pack2(__uint_as_float(r0[g * 8 + 6]) * scale, __uint_as_float(r0[g * 8 + 7]) * scale);
-          dst[g] = w;
+          w.x = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 0]) * scale, __uint_as_float(r0[gq * 8 + 1]) * scale);
+          w.y = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 2]) * scale, __uint_as_float(r0[gq * 8 + 3]) * scale);
+          w.z = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 4]) * scale, __uint_as_float(r0[gq * 8 + 5]) * scale);
+          w.w = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 6]) * scale, __uint_as_float(r0[gq * 8 + 7]) * scale);
+          dst[gq] = w;
         }
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
+        for (int gq = 0; gq < 4; ++gq) {
           uint4 w;
-          w.x = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 0]) * scale, __uint_as_float(r1[g * 8 + 1]) * scale);
-          w.y = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 2]) * scale, __uint_as_float(r1[g * 8 + 3]) * scale);
-          w.z = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 4]) * scale, __uint_as_float(r1[g * 8 + 5]) * scale);
-          w.w = ElemTraits<T>::pack2(__uint_as_float(r1[g * 8 + 6]) * scale, __uint_as_float(r1[g * 8 + 7]) * scale);
-          dst[4 + g] = w;
+          w.x = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 0]) * scale, __uint_as_float(r1[gq * 8 + 1]) * scale);
+          w.y = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 2]) * scale, __uint_as_float(r1[gq * 8 + 3]) * scale);
+          w.z = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 4]) * scale, __uint_as_float(r1[gq * 8 + 5]) * scale);
+          w.w = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 6]) * scale, __uint_as_float(r1[gq * 8 + 7]) * scale);
+          dst[4 + gq] = w;
         }
       }
+      return true;
+    };
+    bool ok = true;
+    for (int k = g; ok && k < n_local; k += 2) {
+      const int i = k >> 1;
+      const int item = item_of(k);
+      const int head = item % kHeads;
+      const int out_row = (active && row < length) ? attn_row(args, item / kHeads, row) : 0;
+      const float gate = (active && row < length) ? __ldg(args.gates + static_cast<long long>(out_row) * kHeads + head) : 0.f;
+      if (!mbar_wait_warp(&s_full[g], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sum = 1.0f;
+      if (active) {
+        // Two passes over S in TMEM, 64 columns at a time (a TMEM load costs
+        // tens of cycles): the row maximum, then exp2, P and the row sum.
+        // Columns >= length (stale, or never written by the N = nc MMA) are
+        // masked.
+        float mxs[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mxs[a] = -INFINITY;
+#pragma unroll
+        for (int c0 = 0; c0 < NCOLS; c0 += 64) {
+          const int width = NCOLS - c0 < 64 ? NCOLS - c0 : 64;
+          uint32_t ra[32], rb[32];
+          tmem_ld32(s_addr + c0, ra);
+          if (width == 64) tmem_ld32(s_addr + c0 + 32, rb);
+          tmem_wait_ld();
+          reg_fence(ra);
+          if (width == 64) reg_fence(rb);
+#pragma unroll
+          for (int q = 0; q < 64; q += 16) {
+            if (q < width) {
+#pragma unroll
+              for (int a = 0; a < 8; ++a) {
+                const int c1 = c0 + q + a, c2i = c0 + q + 8 + a;
+                const float x1 = c1 < length ? __uint_as_float(q < 32 ? ra[q + a] : rb[q - 32 + a]) : -INFINITY;
+                const float x2 = c2i < length ? __uint_as_float(q < 32 ? ra[q + 8 + a] : rb[q - 24 + a]) : -INFINITY;
+                mxs[a] = fmax3(mxs[a], x1, x2);
+              }
+            }
+          }
+        }
+        const float mx =
+            fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
+        const float mscaled = mx * kScaleLog2;
+        const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
+        const float2 nm2 = make_float2(-mscaled, -mscaled);
+        float2 sums[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                          make_float2(0.f, 0.f)};
+        // P of each 64-column chunk goes over S columns that were already read
+        // (P column c holds keys 2c, 2c+1).
+#pragma unroll
+        for (int c0 = 0; c0 < NCOLS; c0 += 64) {
+          const int width = NCOLS - c0 < 64 ? NCOLS - c0 : 64;
+          uint32_t ra[32], rb[32];
+          tmem_ld32(s_addr + c0, ra);
+          if (width == 64) tmem_ld32(s_addr + c0 + 32, rb);
+          tmem_wait_ld();
+          reg_fence(ra);
+          if (width == 64) reg_fence(rb);
+          uint32_t pk[32];
+#pragma unroll
+          for (int q = 0; q < 64; q += 2) {
+            if (q < width) {
+              float v0 = __uint_as_float(q < 32 ? ra[q] : rb[q - 32]);
+              float v1 = __uint_as_float(q < 32 ? ra[q + 1] : rb[q - 31]);
+              if (c0 + q >= length) v0 = -INFINITY;
+              if (c0 + q + 1 >= length) v1 = -INFINITY;
+              const float2 x2 = __ffma2_rn(make_float2(v0, v1), c2, nm2);
+              float2 p2;
+              if (((q >> 1) & 7) < kPolyPairs) {
+                p2 = exp2_poly2(x2);
+              } else {
+                p2.x = ex2_approx(x2.x);
+                p2.y = ex2_approx(x2.y);
+              }
+              sums[(q >> 1) & 3] = __fadd2_rn(sums[(q >> 1) & 3], p2);
+              pk[q / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
+            }
+          }
+          if (width == 64) {
+            tmem_st32(s_addr + c0 / 2, pk);
+          } else {
+            uint32_t w[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) w[q] = pk[q];
+            tmem_st16(s_addr + c0 / 2, w);
+          }
+        }
+        const float2 s01 = __fadd2_rn(__fadd2_rn(sums[0], sums[1]), __fadd2_rn(sums[2], sums[3]));
+        sum = s01.x + s01.y;
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[g]);
+      if (pend_k >= 0 && !write_output()) {
+        ok = false;
+        break;
+      }
+      pend_k = k;
+      pend_row = out_row;
+      pend_head = head;
+      pend_gate = gate;
+      pend_sum = sum;
     }
+    if (ok && pend_k >= 0) write_output();
   }
 
   tc_fence_before();
@@ -719,6 +813,9 @@ cudaError_t launch_items_cols(const CUtensorMap& map, const AttnArgs& args, int 
   }
   const long long items = static_cast<long long>(args.sequences) * kHeads;
   if (items <= 0) return cudaSuccess;
+  // The kernel indexes items and output rows in 32 bits.
+  const long long rows = static_cast<long long>(args.sequences) * args.length;
+  if (items > 0x7FFFFFFFLL || rows > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   const int grid = items < sm_count ? static_cast<int>(items) : sm_count;
   attention_items_kernel<T, NCOLS><<<grid, kItemThreads, ItemSmem::kBytes, stream>>>(map, args);
   return cudaGetLastError();
