@@ -73,27 +73,28 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 constexpr int kPolyPairs = 2;
 
 // ---------------------------------------------------------------------------
-// Long sequences (L > 128): one CTA computes two 128-query tiles (A, B) of one
-// (sequence, head) that share every K/V tile.  Warps 2-5 own tile A, warps 6-9
-// tile B (one query row per thread).  P goes to tensor memory and the PV MMA
-// reads it from there (A operand in TMEM), so P never touches shared memory.
-// O accumulates in TMEM across KV tiles; a row's reference maximum m is raised
-// only when a tile's maximum exceeds it by more than 2^8 in exp2 units, in
-// which case that row of O (TMEM) and its running sum are rescaled --
-// otherwise P = exp2((s - m) c) <= 256 stays exact enough in 16 bits and no O
-// traffic is needed.
+// Long sequences (L > 128): a persistent CTA walks units of two 128-query
+// tiles (A, B) of one (sequence, head), which share every K/V tile.  Warps 2-5
+// own tile A, warps 6-9 tile B (one query row per thread).  Barrier phases
+// and the K/V ring run on across units and Q is double-buffered, so the next
+// unit's Q load and first S overlap this unit's last tiles and output.  P goes
+// to tensor memory and the PV MMA reads it from there (A operand in TMEM), so
+// P never touches shared memory.  O accumulates in TMEM across KV tiles; a
+// row's reference maximum m is raised only when a tile's maximum exceeds it by
+// more than 2^8 in exp2 units, in which case that row of O (TMEM) and its
+// running sum are rescaled -- otherwise P = exp2((s - m) c) <= 256 stays exact
+// enough in 16 bits and no O traffic is needed.
 //
 // The MMA warp runs its loop warp-uniform and issues each MMA under
-// elect.sync, with descriptors advanced by constant offsets: a tcgen05.mma is
-// then issued in a few cycles, well under its 32-64 cycle execution time.
+// elect.sync, with descriptors advanced by constant offsets.
 constexpr int kPairThreads = 320;
 constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int kKvStages = 3;   // K/V ring depth: loads run two tiles ahead of the PV that frees a stage
 
 struct PairSmem {
-  static constexpr int kQ = 0;                         // 2 x 16 KB
-  static constexpr int kK = kQ + 2 * kQBytes;          // kKvStages x 16 KB
+  static constexpr int kQ = 0;                         // 2 buffers x 2 tiles x 16 KB
+  static constexpr int kK = kQ + 4 * kQBytes;          // kKvStages x 16 KB
   static constexpr int kV = kK + kKvStages * kQBytes;  // kKvStages x 16 KB
   static constexpr int kBar = kV + kKvStages * kQBytes;
   static constexpr int kBytes = 1024 + kBar + 256;
@@ -103,9 +104,34 @@ struct PairSmem {
 // P_A [384,448), P_B [448,512) (P: two 16-bit values per column).
 constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
 
+// One unit of the pair kernel: two query tiles of one (sequence, head).
+struct PairUnit {
+  int q0, ntiles, head, c_a, c_b;
+  long long seq;
+};
+
+__device__ __forceinline__ PairUnit pair_unit(const AttnArgs& args, long long u) {
+  const int q_pairs = (args.q_tiles + 1) / 2;
+  PairUnit p;
+  const int pair = static_cast<int>(u % q_pairs);
+  const long long rest = u / q_pairs;
+  p.head = static_cast<int>(rest % kHeads);
+  p.seq = rest / kHeads;
+  p.q0 = pair * 2 * kTile;
+  p.ntiles = (p.q0 + kTile < args.length) ? 2 : 1;
+  if (args.pos_dim == 1) {
+    p.c_a = static_cast<int>(p.seq % args.d2);
+    p.c_b = static_cast<int>(p.seq / args.d2);
+  } else {
+    p.c_a = static_cast<int>(p.seq % args.d1);
+    p.c_b = static_cast<int>(p.seq / args.d1);
+  }
+  return p;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kPairThreads, 1)
-    attention_pair_kernel(const __grid_constant__ CUtensorMap map, const AttnArgs args) {
+    attention_pair_kernel(const __grid_constant__ CUtensorMap map, const AttnArgs args, long long units) {
   using L = PairSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,40 +139,32 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint8_t* sK = smem + L::kK;
   uint8_t* sV = smem + L::kV;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;                 // [kKvStages]
+  uint64_t* q_full = bars;                      // [Q buffer]
+  uint64_t* q_empty = bars + 2;                 // [Q buffer]
+  uint64_t* kv_full = bars + 4;                 // [kKvStages]
   uint64_t* kv_empty = kv_full + kKvStages;     // [kKvStages]
   uint64_t* s_full = kv_empty + kKvStages;      // [tile]
   uint64_t* s_empty = s_full + 2;               // [tile]
   uint64_t* p_full = s_empty + 2;               // [tile]
   uint64_t* o_full = p_full + 2;                // [tile]
-  uint64_t* drain = o_full + 2;
+  uint64_t* o_empty = o_full + 2;               // [tile]
+  uint64_t* drain = o_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const long long bid = blockIdx.x;
-  const int q_pairs = (args.q_tiles + 1) / 2;
-  const int pair = static_cast<int>(bid % q_pairs);
-  const long long rest = bid / q_pairs;
-  const int head = static_cast<int>(rest % kHeads);
-  const long long seq = rest / kHeads;
-  const int q0 = pair * 2 * kTile;
   const int length = args.length;
-  const int ntiles = (q0 + kTile < length) ? 2 : 1;
   const int nkv = (length + kTile - 1) / kTile;
-  int c_a, c_b;
-  if (args.pos_dim == 1) {
-    c_a = static_cast<int>(seq % args.d2);
-    c_b = static_cast<int>(seq / args.d2);
-  } else {
-    c_a = static_cast<int>(seq % args.d1);
-    c_b = static_cast<int>(seq / args.d1);
-  }
+  const int n_local =
+      static_cast<long long>(blockIdx.x) < units ? static_cast<int>((units - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  auto unit_of = [&](int lu) { return static_cast<long long>(blockIdx.x) + static_cast<long long>(lu) * gridDim.x; };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int i = 0; i < kKvStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -156,6 +174,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -173,37 +192,61 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch(&map);
-      auto load_tile = [&](uint8_t* dst, uint64_t* bar, int col, int pos) {
-        if (args.pos_dim == 1)
-          tma_load_4d(dst, &map, bar, col, pos, c_a, c_b);
-        else
-          tma_load_4d(dst, &map, bar, col, c_a, pos, c_b);
-      };
-      mbar_arrive_expect_tx(q_full, ntiles * kQBytes);
-      load_tile(sQ, q_full, head * kDimHead, q0);
-      if (ntiles == 2) load_tile(sQ + kQBytes, q_full, head * kDimHead, q0 + kTile);
-      for (int j = 0; j < nkv; ++j) {
-        const int st = j % kKvStages;
-        const uint32_t par = static_cast<uint32_t>(j / kKvStages) & 1u;
-        if (!mbar_wait(&kv_empty[st], par ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kQBytes);
-        load_tile(sK + st * kQBytes, &kv_full[st], kDimInner + head * kDimHead, j * kTile);
-        load_tile(sV + st * kQBytes, &kv_full[st], 2 * kDimInner + head * kDimHead, j * kTile);
+      int kvc = 0;   // K/V tiles loaded so far (ring position)
+      bool ok = true;
+      for (int lu = 0; ok && lu < n_local; ++lu) {
+        const PairUnit pu = pair_unit(args, unit_of(lu));
+        auto load_tile = [&](uint8_t* dst, uint64_t* bar, int col, int pos) {
+          if (args.pos_dim == 1)
+            tma_load_4d(dst, &map, bar, col, pos, pu.c_a, pu.c_b);
+          else
+            tma_load_4d(dst, &map, bar, col, pu.c_a, pos, pu.c_b);
+        };
+        const int qb = lu & 1;
+        if (!mbar_wait(&q_empty[qb], (static_cast<uint32_t>(lu >> 1) & 1u) ^ 1u, abort_flag, args.err, kErrWaitTma))
+          break;
+        uint8_t* q_dst = sQ + qb * 2 * kQBytes;
+        mbar_arrive_expect_tx(&q_full[qb], pu.ntiles * kQBytes);
+        load_tile(q_dst, &q_full[qb], pu.head * kDimHead, pu.q0);
+        if (pu.ntiles == 2) load_tile(q_dst + kQBytes, &q_full[qb], pu.head * kDimHead, pu.q0 + kTile);
+        for (int j = 0; j < nkv; ++j, ++kvc) {
+          const int st = kvc % kKvStages;
+          const uint32_t par = static_cast<uint32_t>(kvc / kKvStages) & 1u;
+          if (!mbar_wait(&kv_empty[st], par ^ 1u, abort_flag, args.err, kErrWaitTma)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * kQBytes);
+          load_tile(sK + st * kQBytes, &kv_full[st], kDimInner + pu.head * kDimHead, j * kTile);
+          load_tile(sV + st * kQBytes, &kv_full[st], 2 * kDimInner + pu.head * kDimHead, j * kTile);
+        }
       }
     }
   } else if (warp == 1) {
-    // MMA warp: warp-uniform control flow, one elected lane issues.
+    // MMA warp: warp-uniform control flow, one elected lane issues.  Step t =
+    // (unit, KV tile j) issues S(t) and then PV(t-1), which may belong to the
+    // previous unit.
     const uint32_t bf = ElemTraits<T>::kBf16;
     const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
     const uint64_t q_desc = sw128_desc(smem_u32(sQ), 16, 1024);
     const uint64_t k_desc = sw128_desc(smem_u32(sK), 16, 1024);
     const uint64_t v_desc = sw128_desc(smem_u32(sV), 8192, 1024);
-    auto issue_pv = [&](int i) -> bool {
-      const int st = i % kKvStages;
-      const int ksteps = min(kTile, round16(length - i * kTile)) / 16;
-      const uint64_t vd = v_desc + static_cast<uint64_t>((st * kQBytes) >> 4);
-      for (int x = 0; x < ntiles; ++x) {
-        if (!mbar_wait_warp(&p_full[x], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitMma))
+    int sc[2] = {0, 0};   // S MMAs issued per tile
+    int pc[2] = {0, 0};   // PV MMAs issued per tile
+    int uc[2] = {0, 0};   // units whose O has been completed per tile
+    struct Pending {
+      bool valid;
+      int j, ntiles, st;
+    } prev = {false, 0, 0, 0};
+    auto issue_pv = [&](const Pending& pv) -> bool {
+      const int ksteps = min(kTile, round16(length - pv.j * kTile)) / 16;
+      const uint64_t vd = v_desc + static_cast<uint64_t>((pv.st * kQBytes) >> 4);
+      for (int x = 0; x < pv.ntiles; ++x) {
+        if (!mbar_wait_warp(&p_full[x], static_cast<uint32_t>(pc[x]) & 1u, abort_flag, args.err, kErrWaitMma))
+          return false;
+        // The first PV of a unit overwrites O: the previous unit's O must have been read.
+        if (pv.j == 0 && uc[x] > 0 &&
+            !mbar_wait_warp(&o_empty[x], static_cast<uint32_t>(uc[x] - 1) & 1u, abort_flag, args.err, kErrWaitMma))
           return false;
         tc_fence_after();
         if (elect_one()) {
@@ -211,44 +254,63 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint32_t p_col = tmem_base + kColP + x * (kTile / 2);
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk)
-            if (kk < ksteps) umma_f16_ts(o_col, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+            if (kk < ksteps)
+              umma_f16_ts(o_col, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o, (pv.j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&o_full[x]);
         }
         __syncwarp();
+        ++pc[x];
+        if (pv.j == nkv - 1) ++uc[x];
       }
-      if (elect_one()) umma_commit(&kv_empty[st]);
+      if (elect_one()) umma_commit(&kv_empty[pv.st]);
       __syncwarp();
       return true;
     };
-    bool ok = mbar_wait_warp(q_full, 0, abort_flag, args.err, kErrWaitMma);
-    for (int j = 0; ok && j < nkv; ++j) {
-      const int st = j % kKvStages;
-      if (!mbar_wait_warp(&kv_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, args.err,
-                          kErrWaitMma)) {
+    bool ok = true;
+    int kvc = 0;
+    for (int lu = 0; ok && lu < n_local; ++lu) {
+      const PairUnit pu = pair_unit(args, unit_of(lu));
+      const int qb = lu & 1;
+      if (!mbar_wait_warp(&q_full[qb], static_cast<uint32_t>(lu >> 1) & 1u, abort_flag, args.err, kErrWaitMma)) {
         ok = false;
         break;
       }
-      const int nc = min(kTile, round16(length - j * kTile));
-      const uint32_t idesc_s = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
-      const uint64_t kd = k_desc + static_cast<uint64_t>((st * kQBytes) >> 4);
-      for (int x = 0; x < ntiles && ok; ++x) {
-        if (!mbar_wait_warp(&s_empty[x], (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag, args.err, kErrWaitMma)) {
+      for (int j = 0; ok && j < nkv; ++j, ++kvc) {
+        const int st = kvc % kKvStages;
+        if (!mbar_wait_warp(&kv_full[st], static_cast<uint32_t>(kvc / kKvStages) & 1u, abort_flag, args.err,
+                            kErrWaitMma)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        if (elect_one()) {
-          const uint64_t qd = q_desc + static_cast<uint64_t>((x * kQBytes) >> 4);
+        const int nc = min(kTile, round16(length - j * kTile));
+        const uint32_t idesc_s = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
+        const uint64_t kd = k_desc + static_cast<uint64_t>((st * kQBytes) >> 4);
+        for (int x = 0; x < pu.ntiles && ok; ++x) {
+          if (!mbar_wait_warp(&s_empty[x], (static_cast<uint32_t>(sc[x]) & 1u) ^ 1u, abort_flag, args.err,
+                              kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (elect_one()) {
+            const uint64_t qd = q_desc + static_cast<uint64_t>(((qb * 2 + x) * kQBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kDimHead / 16; ++kk)
-            umma_f16(tmem_base + kColS + x * kTile, qd + 2 * kk, kd + 2 * kk, idesc_s, kk != 0 ? 1u : 0u);
-          umma_commit(&s_full[x]);
+            for (int kk = 0; kk < kDimHead / 16; ++kk)
+              umma_f16(tmem_base + kColS + x * kTile, qd + 2 * kk, kd + 2 * kk, idesc_s, kk != 0 ? 1u : 0u);
+            umma_commit(&s_full[x]);
+            if (j == nkv - 1 && x == pu.ntiles - 1) umma_commit(&q_empty[qb]);   // Q buffer free after the last S
+          }
+          __syncwarp();
+          ++sc[x];
         }
-        __syncwarp();
+        if (ok && prev.valid && !issue_pv(prev)) ok = false;
+        prev.valid = true;
+        prev.j = j;
+        prev.ntiles = pu.ntiles;
+        prev.st = st;
       }
-      if (ok && j > 0 && !issue_pv(j - 1)) ok = false;
     }
-    if (ok) issue_pv(nkv - 1);
+    if (ok && prev.valid) issue_pv(prev);
     if (elect_one()) {
       umma_commit(drain);
       wait_drain(drain, 0, args.err);
@@ -262,130 +324,140 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t s_addr = tmem_base + kColS + x * kTile + lane_off;
     const uint32_t o_addr = tmem_base + kColO + x * kDimHead + lane_off;
     const uint32_t p_addr = tmem_base + kColP + x * (kTile / 2) + lane_off;
-    bool ok = x < ntiles;
-    float m_ref = -INFINITY;   // reference maximum (raw score units)
-    float l_run = 0.f;
-    for (int j = 0; ok && j < nkv; ++j) {
-      if (!mbar_wait_warp(&s_full[x], static_cast<uint32_t>(j) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int valid = length - j * kTile;
-      // The tile is processed as two 64-column halves.  The reference maximum
-      // only has to keep exp2 below 2^8, so each half is exponentiated against
-      // the current reference; when the second half raises it, the packed P of
-      // the first half is rescaled.  All 128 S columns are read; columns >=
-      // valid (stale, or never written by a narrower MMA) are masked.
-      uint32_t pk[kTile / 2];   // P packed to 16-bit pairs
-      float sum = 0.f;
-      float factor = 1.0f;      // accumulated rescale of O and l for this tile
-      bool raised = false;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(s_addr + 64 * hh, ra);
-        tmem_ld32(s_addr + 64 * hh + 32, rb);
-        tmem_wait_ld();
-        reg_fence(ra);
-        reg_fence(rb);
-        if (hh == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s_empty[x]);   // S buffer free for the next tile
-        }
-        float v[64];
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          v[q] = __uint_as_float(ra[q]);
-          v[32 + q] = __uint_as_float(rb[q]);
-        }
-        if (valid < kTile) {   // only the last KV tile has keys past the end
-#pragma unroll
-          for (int q = 0; q < 64; ++q)
-            if (64 * hh + q >= valid) v[q] = -INFINITY;
-        }
-        float mxs[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) mxs[a] = v[a];
-#pragma unroll
-        for (int q = 8; q < 64; q += 16)
-#pragma unroll
-          for (int a = 0; a < 8; ++a) mxs[a] = fmax3(mxs[a], v[q + a], v[q + 8 + a]);
-        const float mx = fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
-        // Raise the reference maximum only when this half would exceed 2^8.
-        if ((mx - m_ref) * kScaleLog2 > kRescaleLog2) {
-          const float f = ex2_approx((m_ref - mx) * kScaleLog2);   // 0 when m_ref = -inf
-          m_ref = mx;
-          factor *= f;
-          sum *= f;
-          raised = true;
-          if (hh == 1) {
-            const uint32_t f2 = ElemTraits<T>::pack2(f, f);
-#pragma unroll
-            for (int q = 0; q < 32; ++q) pk[q] = ElemTraits<T>::mul2(pk[q], f2);
-          }
-        }
-        const float mscaled = m_ref * kScaleLog2;
-        const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
-        const float2 nm2 = make_float2(-mscaled, -mscaled);
-        float2 sums[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                          make_float2(0.f, 0.f)};
-#pragma unroll
-        for (int q = 0; q < 64; q += 2) {
-          const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
-          float2 p2;
-          if (((q >> 1) & 7) < kPolyPairs) {
-            p2 = exp2_poly2(x2);
-          } else {
-            p2.x = ex2_approx(x2.x);
-            p2.y = ex2_approx(x2.y);
-          }
-          sums[(q >> 1) & 3] = __fadd2_rn(sums[(q >> 1) & 3], p2);
-          pk[32 * hh + q / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
-        }
-        const float2 s01 = __fadd2_rn(__fadd2_rn(sums[0], sums[1]), __fadd2_rn(sums[2], sums[3]));
-        sum += s01.x + s01.y;
-      }
-      const bool raise = raised;
-      if (j > 0) {
-        // PV of the previous tile must be complete before P is overwritten and
-        // before this row of O is rescaled.
-        if (!mbar_wait_warp(&o_full[x], static_cast<uint32_t>(j - 1) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
+    int c = 0;   // S tiles consumed by this tile slot so far
+    bool ok = true;
+    for (int lu = 0; ok && lu < n_local; ++lu) {
+      const PairUnit pu = pair_unit(args, unit_of(lu));
+      if (x >= pu.ntiles) continue;
+      float m_ref = -INFINITY;   // reference maximum (raw score units)
+      float l_run = 0.f;
+      for (int j = 0; ok && j < nkv; ++j, ++c) {
+        if (!mbar_wait_warp(&s_full[x], static_cast<uint32_t>(c) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, raise)) {
+        const int valid = length - j * kTile;
+        // The tile is processed as two 64-column halves.  The reference maximum
+        // only has to keep exp2 below 2^8, so each half is exponentiated against
+        // the current reference; when the second half raises it, the packed P of
+        // the first half is rescaled.  All 128 S columns are read; columns >=
+        // valid (stale, or never written by a narrower MMA) are masked.
+        uint32_t pk[kTile / 2];   // P packed to 16-bit pairs
+        float sum = 0.f;
+        float factor = 1.0f;      // accumulated rescale of O and l for this tile
+        bool raised = false;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t r[32];
-            tmem_ld32(o_addr + half * 32, r);
-            tmem_wait_ld();
-            reg_fence(r);
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(s_addr + 64 * hh, ra);
+          tmem_ld32(s_addr + 64 * hh + 32, rb);
+          tmem_wait_ld();
+          reg_fence(ra);
+          reg_fence(rb);
+          if (hh == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[x]);   // S buffer free for the next tile
+          }
+          float v[64];
 #pragma unroll
-            for (int d = 0; d < 32; ++d) r[d] = __float_as_uint(__uint_as_float(r[d]) * factor);
-            tmem_st32(o_addr + half * 32, r);
+          for (int q = 0; q < 32; ++q) {
+            v[q] = __uint_as_float(ra[q]);
+            v[32 + q] = __uint_as_float(rb[q]);
+          }
+          if (valid < kTile) {   // only the last KV tile has keys past the end
+#pragma unroll
+            for (int q = 0; q < 64; ++q)
+              if (64 * hh + q >= valid) v[q] = -INFINITY;
+          }
+          float mxs[8];
+#pragma unroll
+          for (int a = 0; a < 8; ++a) mxs[a] = v[a];
+#pragma unroll
+          for (int q = 8; q < 64; q += 16)
+#pragma unroll
+            for (int a = 0; a < 8; ++a) mxs[a] = fmax3(mxs[a], v[q + a], v[q + 8 + a]);
+          const float mx = fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
+          // Raise the reference maximum only when this half would exceed 2^8.
+          if ((mx - m_ref) * kScaleLog2 > kRescaleLog2) {
+            const float f = ex2_approx((m_ref - mx) * kScaleLog2);   // 0 when m_ref = -inf
+            m_ref = mx;
+            factor *= f;
+            sum *= f;
+            raised = true;
+            if (hh == 1) {
+              const uint32_t f2 = ElemTraits<T>::pack2(f, f);
+#pragma unroll
+              for (int q = 0; q < 32; ++q) pk[q] = ElemTraits<T>::mul2(pk[q], f2);
+            }
+          }
+          const float mscaled = m_ref * kScaleLog2;
+          const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
+          const float2 nm2 = make_float2(-mscaled, -mscaled);
+          float2 sums[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                            make_float2(0.f, 0.f)};
+#pragma unroll
+          for (int q = 0; q < 64; q += 2) {
+            const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
+            float2 p2;
+            if (((q >> 1) & 7) < kPolyPairs) {
+              p2 = exp2_poly2(x2);
+            } else {
+              p2.x = ex2_approx(x2.x);
+              p2.y = ex2_approx(x2.y);
+            }
+            sums[(q >> 1) & 3] = __fadd2_rn(sums[(q >> 1) & 3], p2);
+            pk[32 * hh + q / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
+          }
+          const float2 s01 = __fadd2_rn(__fadd2_rn(sums[0], sums[1]), __fadd2_rn(sums[2], sums[3]));
+          sum += s01.x + s01.y;
+        }
+        const bool raise = raised;
+        if (c > 0) {
+          // PV of the previous tile must be complete before P is overwritten
+          // and (within a unit) before this row of O is rescaled.
+          if (!mbar_wait_warp(&o_full[x], static_cast<uint32_t>(c - 1) & 1u, abort_flag, args.err,
+                              kErrWaitSoftmax)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (j > 0 && __any_sync(0xffffffffu, raise)) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              uint32_t r[32];
+              tmem_ld32(o_addr + half * 32, r);
+              tmem_wait_ld();
+              reg_fence(r);
+#pragma unroll
+              for (int d = 0; d < 32; ++d) r[d] = __float_as_uint(__uint_as_float(r[d]) * factor);
+              tmem_st32(o_addr + half * 32, r);
+            }
           }
         }
-      }
-      l_run = l_run * factor + sum;
-      {
-        uint32_t p0[32], p1[32];
+        l_run = l_run * factor + sum;
+        {
+          uint32_t p0[32], p1[32];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          p0[q] = pk[q];
-          p1[q] = pk[32 + q];
+          for (int q = 0; q < 32; ++q) {
+            p0[q] = pk[q];
+            p1[q] = pk[32 + q];
+          }
+          tmem_st32(p_addr, p0);
+          tmem_st32(p_addr + 32, p1);
         }
-        tmem_st32(p_addr, p0);
-        tmem_st32(p_addr + 32, p1);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[x]);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[x]);
-    }
-    if (ok && mbar_wait_warp(&o_full[x], static_cast<uint32_t>(nkv - 1) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
+      if (!ok) break;
+      // Unit output: wait for the last PV, read O, release it, store.
+      if (!mbar_wait_warp(&o_full[x], static_cast<uint32_t>(c - 1) & 1u, abort_flag, args.err, kErrWaitSoftmax)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t r0[32], r1[32];
       tmem_ld32(o_addr, r0);
@@ -393,15 +465,18 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tmem_wait_ld();
       reg_fence(r0);
       reg_fence(r1);
-      const int qpos = q0 + x * kTile + row;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[x]);
+      const int qpos = pu.q0 + x * kTile + row;
       if (qpos < length) {
         long long R;
         if (args.pos_dim == 1)
-          R = seq * args.d1 + qpos;
+          R = pu.seq * args.d1 + qpos;
         else
-          R = (static_cast<long long>(c_b) * args.d2 + qpos) * args.d1 + c_a;
-        const float scale = __ldg(args.gates + R * kHeads + head) / l_run;
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(args.out) + R * kDimInner + head * kDimHead);
+          R = (static_cast<long long>(pu.c_b) * args.d2 + qpos) * args.d1 + pu.c_a;
+        const float scale = __ldg(args.gates + R * kHeads + pu.head) / l_run;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(args.out) + R * kDimInner + pu.head * kDimHead);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           uint4 w;
@@ -433,7 +508,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 }
 
 template <typename T>
-cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, cudaStream_t stream) {
+cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, int sm_count, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(attention_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -441,10 +516,10 @@ cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, cudaStream
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const long long blocks = static_cast<long long>((args.q_tiles + 1) / 2) * kHeads * args.sequences;
-  if (blocks <= 0) return cudaSuccess;
-  if (blocks > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
-  attention_pair_kernel<T><<<static_cast<unsigned>(blocks), kPairThreads, PairSmem::kBytes, stream>>>(map, args);
+  const long long units = static_cast<long long>((args.q_tiles + 1) / 2) * kHeads * args.sequences;
+  if (units <= 0) return cudaSuccess;
+  const int grid = units < sm_count ? static_cast<int>(units) : sm_count;
+  attention_pair_kernel<T><<<grid, kPairThreads, PairSmem::kBytes, stream>>>(map, args, units);
   return cudaGetLastError();
 }
 
@@ -836,8 +911,9 @@ cudaError_t launch_attention(bool bf16, const CUtensorMap& map_qkv, const AttnAr
   const bool single = args.length <= kTile;
   if (bf16)
     return single ? launch_items<__nv_bfloat16>(map_qkv, args, sm_count, stream)
-                  : launch_pair<__nv_bfloat16>(map_qkv, args, stream);
-  return single ? launch_items<__half>(map_qkv, args, sm_count, stream) : launch_pair<__half>(map_qkv, args, stream);
+                  : launch_pair<__nv_bfloat16>(map_qkv, args, sm_count, stream);
+  return single ? launch_items<__half>(map_qkv, args, sm_count, stream)
+                : launch_pair<__half>(map_qkv, args, sm_count, stream);
 }
 
 }  // namespace vab
