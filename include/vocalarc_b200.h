@@ -55,6 +55,38 @@ int vocalarc_b200_take_device_error(native_gpu *gpu);
 /* 0 = fp16 operands (default), 1 = bf16 operands; both accumulate in fp32. */
 int vocalarc_b200_set_precision(native_gpu *gpu, int bf16);
 
+/* ---- One track's chunks sharded across GPUs (one provider per GPU).
+   The chunk plan of vocalarc_b200_separate_chunked is split into contiguous
+   ranges of at least two chunks.  A range owns the padded samples
+   [chunk_begin * step, chunk_end * step) (the last range: to the padded end);
+   only its seam -- the partial overlap-add sums of the `seam` = chunk - step
+   samples its last chunk reaches past that -- crosses to the next range, by a
+   peer copy over NVLink.  The merged output is bit-identical to
+   vocalarc_b200_separate_chunked.  Sequence per range:
+     range_forward -> (next range: seam_import or seam_from) -> range_finish. */
+
+/* Chunk plan for a track of `length` samples (chunk_samples <= 0 selects 881559). */
+int vocalarc_b200_chunk_plan(int length, int chunk_samples, int *chunks, int *step, int *border,
+                             int *seam);
+/* Forward of chunks [chunk_begin, chunk_end) of the device track d_audio
+   ([2][length]); keeps the chunk outputs and computes this range's seam.
+   Returns after the seam is complete on the device. */
+int vocalarc_b200_range_forward(native_gpu *gpu, const float *d_audio, int length, int chunk_samples,
+                                int model_batch, int chunk_begin, int chunk_end);
+/* Output samples [*s0, *s1) this range writes in range_finish. */
+int vocalarc_b200_range_owned(const native_gpu *gpu, int *s0, int *s1);
+/* CUDA IPC handle (64 bytes) of this range's seam, for the next range's
+   process.  The seam stays valid until this provider's next range_forward. */
+int vocalarc_b200_range_seam_export(native_gpu *gpu, void *handle);
+/* Copies the previous range's seam from its exported handle (another process,
+   any GPU of the node) into this GPU's memory. */
+int vocalarc_b200_range_seam_import(native_gpu *gpu, const void *handle);
+/* Same, from a provider of this process (same or another GPU). */
+int vocalarc_b200_range_seam_from(native_gpu *gpu, const native_gpu *prev);
+/* Writes this range's output samples into the device buffer d_vocals
+   ([2][length]); other samples are not touched. */
+int vocalarc_b200_range_finish(native_gpu *gpu, float *d_vocals);
+
 /* Number of kernels this provider has launched (all streams it owns). */
 long long vocalarc_b200_launch_count(const native_gpu *gpu);
 /* Launch trace: after trace_begin every launch records a CUDA event on the

@@ -206,6 +206,14 @@ struct native_gpu {
   long long resident_tokens = 0;
   int phys_s = 0, phys_l = 0;   // layout of the device buffer: [phys_s][phys_l]
   int transposed = 0;           // logical layout = [phys_l][phys_s] when set
+  // one chunk range of a track sharded across GPUs (vocalarc_b200_range_*)
+  int range_ready = 0;          // range_forward completed; finish may run
+  int range_length = 0, range_chunk = 0, range_step = 0, range_border = 0, range_plen = 0;
+  int range_chunks = 0, range_batch = 1, range_c0 = 0, range_c1 = 0;
+  float* seam_out = nullptr;    // partial sums past this range ([3][seam])
+  float* seam_in = nullptr;     // the previous range's seam, copied here
+  long long seam_cap = 0;       // floats allocated in each seam buffer
+  int has_seam_in = 0;
   // launch trace: one event after every launch on the provider stream
   long long launches = 0;
   int trace = 0;
@@ -851,7 +859,7 @@ void native_gpu_destroy(native_gpu* g) {
   if (g->stream != nullptr) cudaStreamSynchronize(g->stream);
   void* ptrs[] = {g->x, g->x_alt, g->x16, g->row_inv, g->qkv, g->attn, g->gates, g->spec, g->mask, g->frames_buf,
                   g->seg_out, g->audio_in, g->audio_out, g->d_tiles1, g->d_tiles2, g->d_err, g->d_window,
-                  g->d_twiddle, g->d_rope, g->abi_mask_mem};
+                  g->d_twiddle, g->d_rope, g->abi_mask_mem, g->seam_out, g->seam_in};
   for (void* p : ptrs)
     if (p != nullptr) cudaFree(p);
   for (auto& e : g->block_cache) cudaFree(e.mem);
@@ -1140,6 +1148,156 @@ int vocalarc_b200_separate(native_gpu* g, const float* audio, int length, float*
 int vocalarc_b200_separate_chunked(native_gpu* g, const float* audio, int length, int chunk_samples, int model_batch,
                                    float* vocals) {
   return separate_host(g, audio, length, 1, chunk_samples, model_batch, vocals);
+}
+
+// ------------------------------------------------------------------ chunk ranges
+// One track's chunks split into contiguous ranges, one per GPU.  A range owns
+// the padded samples [c0 * step, c1 * step) (the last range: to the padded
+// end); its last chunk reaches `seam` = chunk - step samples further, and those
+// partial overlap-add sums are the only data that crosses to the next range.
+
+int vocalarc_b200_chunk_plan(int length, int chunk_samples, int* chunks, int* step, int* border, int* seam) {
+  if (length <= 0) return 0;
+  const int chunk = chunk_samples > 0 ? chunk_samples : 881559;
+  const int st = chunk / 2;
+  const int bd = chunk - st;
+  const bool padded = length > 2 * bd && bd > 0;
+  const long long plen = padded ? static_cast<long long>(length) + 2 * bd : length;
+  if (st <= 0 || plen > 0x7FFFFFFFLL) return 0;
+  if (chunks != nullptr) *chunks = static_cast<int>((plen + st - 1) / st);
+  if (step != nullptr) *step = st;
+  if (border != nullptr) *border = padded ? bd : 0;
+  if (seam != nullptr) *seam = chunk - st;
+  return 1;
+}
+
+int vocalarc_b200_range_forward(native_gpu* g, const float* d_audio, int length, int chunk_samples, int model_batch,
+                                int chunk_begin, int chunk_end) {
+  if (!active(g) || d_audio == nullptr) return 0;
+  if (!g->model_loaded) {
+    fprintf(stderr, "vocalarc-b200: no model loaded (vocalarc_b200_load_model)\n");
+    return 0;
+  }
+  int chunks = 0, step = 0, border = 0, seam = 0;
+  if (!vocalarc_b200_chunk_plan(length, chunk_samples, &chunks, &step, &border, &seam)) return 0;
+  // Ranges hold at least two chunks (unless one range covers the track), so a
+  // seam only ever crosses to the next range.
+  if (chunk_begin < 0 || chunk_end > chunks || chunk_end - chunk_begin < (chunk_end - chunk_begin == chunks ? 1 : 2)) {
+    fprintf(stderr, "vocalarc-b200: chunk range [%d, %d) invalid for %d chunks (ranges need >= 2 chunks)\n",
+            chunk_begin, chunk_end, chunks);
+    return 0;
+  }
+  cudaSetDevice(g->device);
+  const int chunk = chunk_samples > 0 ? chunk_samples : 881559;
+  const int frames = chunk / kHop + 1;
+  const int plen = border > 0 ? length + 2 * border : length;
+  const int n = chunk_end - chunk_begin;
+  g->range_ready = 0;
+  g->has_seam_in = 0;
+  if (!ensure_seg(g, static_cast<long long>(n) * 2 * chunk)) return 0;
+  if (g->seam_cap < 3ll * seam) {
+    g->seam_cap = 0;
+    if (!grow(g, &g->seam_out, static_cast<size_t>(seam) * 3 * 4, "cudaMalloc(seam_out)") ||
+        !grow(g, &g->seam_in, static_cast<size_t>(seam) * 3 * 4, "cudaMalloc(seam_in)"))
+      return 0;
+    g->seam_cap = 3ll * seam;
+  }
+  const int per_pass = max_segments(g, frames, chunk);
+  for (int c = chunk_begin; c < chunk_end; c += per_pass) {
+    const int m = chunk_end - c < per_pass ? chunk_end - c : per_pass;
+    const SegmentMap mm = demix_map(length, chunk, border, plen, step, c);
+    if (!forward_segments(g, d_audio, mm, m, frames, g->seg_out + static_cast<long long>(c - chunk_begin) * 2 * chunk))
+      return 0;
+  }
+  g->range_length = length;
+  g->range_chunk = chunk;
+  g->range_step = step;
+  g->range_border = border;
+  g->range_plen = plen;
+  g->range_chunks = chunks;
+  g->range_batch = model_batch < 1 ? 1 : model_batch;
+  g->range_c0 = chunk_begin;
+  g->range_c1 = chunk_end;
+  if (chunk_end < chunks) {
+    const SegmentMap dm = demix_map(length, chunk, border, plen, step, 0);
+    DemixRange r{chunk_begin, chunk_end, chunk_end * step, chunk_end * step + seam, nullptr, 0, 0, g->seam_out, nullptr};
+    if (!launched(g, launch_demix_range(g->seg_out, dm, chunks, g->range_batch, r, g->stream), "demix seam")) return 0;
+  }
+  // The seam is read by another provider or process once this returns.
+  if (!sync_and_check(g, "range forward")) return 0;
+  g->range_ready = 1;
+  return 1;
+}
+
+int vocalarc_b200_range_owned(const native_gpu* g, int* s0, int* s1) {
+  if (!active(g) || !g->range_ready) return 0;
+  const int p0 = g->range_c0 * g->range_step;
+  const int p1 = g->range_c1 < g->range_chunks ? g->range_c1 * g->range_step : g->range_plen;
+  const int a = p0 - g->range_border, b = p1 - g->range_border;
+  if (s0 != nullptr) *s0 = a < 0 ? 0 : (a > g->range_length ? g->range_length : a);
+  if (s1 != nullptr) *s1 = b < 0 ? 0 : (b > g->range_length ? g->range_length : b);
+  return 1;
+}
+
+int vocalarc_b200_range_seam_export(native_gpu* g, void* handle) {
+  if (!active(g) || !g->range_ready || handle == nullptr || g->range_c1 >= g->range_chunks) return 0;
+  cudaSetDevice(g->device);
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  return cuda_ok(g, cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), g->seam_out),
+                 "cudaIpcGetMemHandle(seam)")
+             ? 1
+             : 0;
+}
+
+int vocalarc_b200_range_seam_import(native_gpu* g, const void* handle) {
+  if (!active(g) || !g->range_ready || handle == nullptr || g->range_c0 == 0) return 0;
+  cudaSetDevice(g->device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* peer = nullptr;
+  if (!cuda_ok(g, cudaIpcOpenMemHandle(&peer, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle(seam)"))
+    return 0;
+  const size_t bytes = static_cast<size_t>(g->range_chunk - g->range_step) * 3 * 4;
+  // Peer copy over NVLink into this GPU's memory; the previous range's
+  // provider keeps the buffer until every range has finished.
+  const bool ok = cuda_ok(g, cudaMemcpyAsync(g->seam_in, peer, bytes, cudaMemcpyDefault, g->stream), "seam copy") &&
+                  sync_and_check(g, "seam copy");
+  cudaIpcCloseMemHandle(peer);
+  if (!ok) return 0;
+  g->has_seam_in = 1;
+  return 1;
+}
+
+int vocalarc_b200_range_seam_from(native_gpu* g, const native_gpu* prev) {
+  if (!active(g) || !g->range_ready || !active(prev) || !prev->range_ready || g->range_c0 == 0 ||
+      prev->range_c1 != g->range_c0)
+    return 0;
+  cudaSetDevice(g->device);
+  const size_t bytes = static_cast<size_t>(g->range_chunk - g->range_step) * 3 * 4;
+  const cudaError_t e = prev->device == g->device
+                            ? cudaMemcpyAsync(g->seam_in, prev->seam_out, bytes, cudaMemcpyDeviceToDevice, g->stream)
+                            : cudaMemcpyPeerAsync(g->seam_in, g->device, prev->seam_out, prev->device, bytes, g->stream);
+  if (!cuda_ok(g, e, "seam copy") || !sync_and_check(g, "seam copy")) return 0;
+  g->has_seam_in = 1;
+  return 1;
+}
+
+int vocalarc_b200_range_finish(native_gpu* g, float* d_vocals) {
+  if (!active(g) || !g->range_ready || d_vocals == nullptr) return 0;
+  if (g->range_c0 > 0 && !g->has_seam_in) {
+    fprintf(stderr, "vocalarc-b200: range [%d, %d) finished without the previous range's seam\n", g->range_c0,
+            g->range_c1);
+    return 0;
+  }
+  cudaSetDevice(g->device);
+  const int seam = g->range_chunk - g->range_step;
+  const SegmentMap dm = demix_map(g->range_length, g->range_chunk, g->range_border, g->range_plen, g->range_step, 0);
+  const int p0 = g->range_c0 * g->range_step;
+  const int p1 = g->range_c1 < g->range_chunks ? g->range_c1 * g->range_step : g->range_plen;
+  DemixRange r{g->range_c0, g->range_c1, p0, p1, g->range_c0 > 0 ? g->seam_in : nullptr, p0, seam, nullptr, d_vocals};
+  if (!launched(g, launch_demix_range(g->seg_out, dm, g->range_chunks, g->range_batch, r, g->stream), "demix range"))
+    return 0;
+  return sync_and_check(g, "range finish") ? 1 : 0;
 }
 
 int vocalarc_b200_synchronize(native_gpu* g) {

@@ -329,6 +329,60 @@ __global__ void transpose_tokens_kernel(const float* __restrict__ src, float* __
   b[threadIdx.x] = a[threadIdx.x];
 }
 
+// Demix over a contiguous chunk range [c0, c1) of the track (sharding of one
+// track across GPUs).  The accumulators of padded sample p start from `init`
+// (the previous range's partial sums for its seam, or zero) and add this
+// range's chunks in ascending order -- the summation order of demix_kernel, so
+// the sharded result is bit-identical to the single-GPU demix.  With seam_out
+// set the partial sums (channel 0, channel 1, weight) are written instead of
+// the divided, cropped output.
+__global__ void __launch_bounds__(256) demix_range_kernel(const float* __restrict__ seg_out, SegmentMap map,
+                                                          int chunks, int model_batch, DemixRange r) {
+  const int p = r.p0 + static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (p >= r.p1) return;
+  const int chunk = map.seg_length;
+  const int fade = chunk / 10;
+  const int c_hi = min(chunks - 1, p / map.step);
+  int c_lo = (p - chunk) / map.step + 1;
+  if (p - chunk < 0) c_lo = 0;
+  const int batches = (chunks + model_batch - 1) / model_batch;
+  const int final_first = (batches - 1) * model_batch;
+  const bool first_forced = model_batch == 1 || chunks == 1;
+  float res0 = 0.f, res1 = 0.f, cnt = 0.f;
+  const int k = p - r.init_p0;
+  if (r.init != nullptr && k >= 0 && k < r.init_len) {
+    res0 = r.init[k];
+    res1 = r.init[r.init_len + k];
+    cnt = r.init[2 * r.init_len + k];
+  }
+  for (int c = max(c_lo, r.c0); c <= min(c_hi, r.c1 - 1); ++c) {
+    const int start = c * map.step;
+    const int valid = min(chunk, map.padded - start);
+    const int i = p - start;
+    if (i < 0 || i >= valid) continue;
+    float w = 1.0f;
+    const bool forced = (c == 0 && first_forced) || c >= final_first;
+    if (!forced && i >= chunk - fade) w = 1.0f - static_cast<float>(i - (chunk - fade)) / static_cast<float>(fade);
+    const float* o = seg_out + static_cast<long long>(c - r.c0) * 2 * chunk;
+    res0 += o[i] * w;
+    res1 += o[chunk + i] * w;
+    cnt += w;
+  }
+  if (r.seam_out != nullptr) {
+    const int len = r.p1 - r.p0;
+    const int j = p - r.p0;
+    r.seam_out[j] = res0;
+    r.seam_out[len + j] = res1;
+    r.seam_out[2 * len + j] = cnt;
+  } else {
+    const int s = p - map.border;
+    if (s >= 0 && s < map.clip_length) {
+      r.vocals[s] = res0 / fmaxf(cnt, 1.0e-12f);
+      r.vocals[static_cast<long long>(map.clip_length) + s] = res1 / fmaxf(cnt, 1.0e-12f);
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int frames, const float* window,
@@ -387,6 +441,13 @@ cudaError_t launch_demix(const float* seg_out, SegmentMap map, int chunks, int m
   if (map.clip_length <= 0) return cudaSuccess;
   dim3 grid((map.clip_length + 255) / 256, 2);
   demix_kernel<<<grid, 256, 0, stream>>>(seg_out, map, chunks, model_batch, vocals);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_demix_range(const float* seg_out, SegmentMap map, int chunks, int model_batch,
+                               const DemixRange& range, cudaStream_t stream) {
+  if (range.p1 <= range.p0) return cudaSuccess;
+  demix_range_kernel<<<(range.p1 - range.p0 + 255) / 256, 256, 0, stream>>>(seg_out, map, chunks, model_batch, range);
   return cudaGetLastError();
 }
 

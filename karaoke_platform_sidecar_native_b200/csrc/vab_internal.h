@@ -138,6 +138,21 @@ cudaError_t launch_overlap_add(const float* frames_buf, int segments, int frames
                                const float* window, float* seg_out, cudaStream_t stream);
 cudaError_t launch_demix(const float* seg_out, SegmentMap map, int chunks, int model_batch,
                          float* vocals, cudaStream_t stream);
+// One contiguous chunk range of a track sharded across GPUs: padded samples
+// [p0, p1), accumulators initialised from `init` ([3][init_len]: channel 0,
+// channel 1, weight; padded sample init_p0 first) where present.  Writes the
+// partial sums to seam_out ([3][p1 - p0]) when set, else the divided, cropped
+// samples to vocals ([2][clip_length]).
+struct DemixRange {
+  int c0, c1;
+  int p0, p1;
+  const float* init;
+  int init_p0, init_len;
+  float* seam_out;
+  float* vocals;
+};
+cudaError_t launch_demix_range(const float* seg_out, SegmentMap map, int chunks, int model_batch,
+                               const DemixRange& range, cudaStream_t stream);
 cudaError_t launch_transpose_tokens(const float* src, float* dst, int s0, int l0, cudaStream_t stream);
 cudaError_t upload_band_tables(const int* first, const int* dims);
 

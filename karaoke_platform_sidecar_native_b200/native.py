@@ -22,6 +22,7 @@ HEADERS = (os.path.join(ROOT, "include", "native_gpu.h"), os.path.join(ROOT, "in
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _vp = ctypes.c_void_p
+_ip = ctypes.POINTER(ctypes.c_int)
 
 
 class TransformerWeights(ctypes.Structure):
@@ -72,6 +73,14 @@ _SIGNATURES = {
     "vocalarc_b200_trace_end": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int]),
     "vocalarc_b200_stage_gemm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int,
                                                 ctypes.c_int, _vp, _vp]),
+    "vocalarc_b200_chunk_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _ip, _ip, _ip, _ip]),
+    "vocalarc_b200_range_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                   ctypes.c_int]),
+    "vocalarc_b200_range_owned": (ctypes.c_int, [_vp, _ip, _ip]),
+    "vocalarc_b200_range_seam_export": (ctypes.c_int, [_vp, _vp]),
+    "vocalarc_b200_range_seam_import": (ctypes.c_int, [_vp, _vp]),
+    "vocalarc_b200_range_seam_from": (ctypes.c_int, [_vp, _vp]),
+    "vocalarc_b200_range_finish": (ctypes.c_int, [_vp, _vp]),
     "vocalarc_b200_stage_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                      ctypes.c_int]),
     "vocalarc_b200_stage_stft": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
@@ -83,6 +92,15 @@ _SIGNATURES = {
 }
 
 _LIB = None
+
+
+def chunk_plan(length: int, chunk: int = 0) -> dict:
+    """Chunk plan of vocalarc_b200_separate_chunked (chunks, step, border, seam)."""
+    lib = load()
+    vals = [ctypes.c_int(0) for _ in range(4)]
+    if not lib.vocalarc_b200_chunk_plan(length, chunk, *[ctypes.byref(v) for v in vals]):
+        raise ProviderError(f"chunk_plan({length}, {chunk}) failed")
+    return dict(zip(("chunks", "step", "border", "seam"), (v.value for v in vals)))
 
 
 def declared_functions() -> list:
@@ -214,6 +232,32 @@ class Provider:
             name, count, ms = line.split("\t")
             out[name] = (int(count), float(ms))
         return out
+
+    # ---- one track's chunks sharded across providers (chunk ranges) -----
+    def range_forward(self, d_audio, length: int, chunk_begin: int, chunk_end: int, chunk: int = 0,
+                      model_batch: int = 1):
+        self.check(self.lib.vocalarc_b200_range_forward(self.handle, dptr(d_audio), length, chunk, model_batch,
+                                                        chunk_begin, chunk_end), "range_forward")
+
+    def range_owned(self) -> tuple:
+        s0, s1 = ctypes.c_int(0), ctypes.c_int(0)
+        self.check(self.lib.vocalarc_b200_range_owned(self.handle, ctypes.byref(s0), ctypes.byref(s1)), "range_owned")
+        return s0.value, s1.value
+
+    def range_seam_export(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        self.check(self.lib.vocalarc_b200_range_seam_export(self.handle, buf), "range_seam_export")
+        return buf.raw
+
+    def range_seam_import(self, handle: bytes):
+        buf = ctypes.create_string_buffer(bytes(handle), 64)
+        self.check(self.lib.vocalarc_b200_range_seam_import(self.handle, buf), "range_seam_import")
+
+    def range_seam_from(self, prev: "Provider"):
+        self.check(self.lib.vocalarc_b200_range_seam_from(self.handle, prev.handle), "range_seam_from")
+
+    def range_finish(self, d_vocals):
+        self.check(self.lib.vocalarc_b200_range_finish(self.handle, dptr(d_vocals)), "range_finish")
 
     # ---- stages (device pointers) --------------------------------------
     def stage_gemm(self, epilogue, a, b, m, n, k, bias, out):
