@@ -249,6 +249,8 @@ def main():
     parser.add_argument("--reference-sample-seconds", type=float, default=1.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--precision", default="fp16", choices=("fp16", "bf16"))
+    parser.add_argument("--shard", action="store_true",
+                        help="strong scaling: one track's chunks sharded across the ranks, seams by CUDA IPC")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -257,6 +259,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
+    if args.shard:
+        return run_shard(args, rank, world, local_rank)
 
     import torch
     import torch.distributed as dist
@@ -401,6 +405,85 @@ def main():
             "kernels": kernels,
             "cpu_baseline": cpu,
             "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    provider.close()
+    return 0
+
+
+def run_shard(args, rank, world, local_rank):
+    """One cfg2 track, its chunks split across the ranks (chunk scheduler).
+
+    Each rank runs its chunk range, the overlap-add seams cross by CUDA IPC peer
+    copy and every rank writes its own output samples.  The process group is
+    gloo: it carries only the 64-byte IPC handles, barriers and the timing max.
+    A step is the whole track; the timed region per rank is CUDA events on the
+    provider stream bracketing the step (host waits for neighbours included).
+    """
+    import torch
+    import torch.distributed as dist
+
+    from karaoke_platform_sidecar_native_b200 import native, shard
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    provider = native.Provider(local_rank)
+    if args.precision == "bf16":
+        provider.set_precision(True)
+    provider.load_model(modelpack.synthetic_pack(**modelpack.BENCH_RECIPE))
+    length = int(args.seconds * 44100)
+    audio = fixtures.long_mix(args.seconds, seed=1)
+    d_audio = torch.from_numpy(audio).cuda()
+    d_vocals = torch.zeros_like(d_audio)
+    plan = native.chunk_plan(length, CHUNK)
+    stream = torch.cuda.ExternalStream(provider.stream)
+
+    def step():
+        if world > 1:
+            return shard.separate_range(provider, d_audio, length, rank, world, chunk=CHUNK, d_vocals=d_vocals,
+                                        plan=plan)
+        provider.separate_device(d_audio, 1, length, d_vocals, chunked=True, chunk=CHUNK, model_batch=1)
+        provider.synchronize()
+        return (0, length)
+
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    launches0 = provider.launch_count
+    start.record(stream)
+    for _ in range(args.steps):
+        owned = step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    launches = provider.launch_count - launches0
+    elapsed_ms = start.elapsed_time(stop)
+    t = torch.tensor([elapsed_ms])
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    value = args.seconds * args.steps / (elapsed_ms / 1000.0)
+    ranges = shard.chunk_ranges(plan["chunks"], world)
+    if rank == 0:
+        line = {
+            "metric": METRIC + " [one track sharded]", "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": args.precision,
+            "data": "synthetic",
+            "config": {"workload": f"cfg2: one {args.seconds:g} s track, {plan['chunks']} chunks sharded as {ranges}",
+                       "seam_samples": plan["seam"], "exchange": "CUDA IPC peer copy of one 3 x seam fp32 buffer "
+                                                               "per range boundary",
+                       "parallelism": f"chunk ranges x{world}"},
+            "gpu_launches": int(launches), "rank0_owned_samples": list(owned),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
