@@ -55,8 +55,10 @@ def load_peaks():
     if os.path.exists(path):
         p = json.load(open(path))
         return {"hbm_gbs": p["hbm_gbs"], "tflops": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "tflops_burst": p["bf16_tflops"],
                 "source": "measured (MEASURED_PEAKS.json; sustained bf16 for kernels inside a long step)"}
-    return {"hbm_gbs": 6650.0, "tflops": 1400.0, "source": "fallback (6.65 TB/s, 1.4 PFLOP/s sustained)"}
+    return {"hbm_gbs": 6650.0, "tflops": 1400.0, "tflops_burst": 1590.0,
+            "source": "fallback (6.65 TB/s, 1.4 PFLOP/s sustained)"}
 
 
 def chunk_count(length):
@@ -249,6 +251,8 @@ def main():
     parser.add_argument("--reference-sample-seconds", type=float, default=1.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--precision", default="fp16", choices=("fp16", "bf16"))
+    parser.add_argument("--ops", action="store_true",
+                        help="config-4 op-level lines: time/band attention, STFT, band split")
     parser.add_argument("--shard", action="store_true",
                         help="strong scaling: one track's chunks sharded across the ranks, seams by CUDA IPC")
     args = parser.parse_args()
@@ -261,6 +265,8 @@ def main():
         return run_reference_arm(args, rank, world)
     if args.shard:
         return run_shard(args, rank, world, local_rank)
+    if args.ops:
+        return run_ops(args)
 
     import torch
     import torch.distributed as dist
@@ -411,6 +417,78 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     provider.close()
+    return 0
+
+
+def run_ops(args):
+    """Config 4 (op-level microbenchmarks, seeded N(0,1) inputs in bf16), one JSON
+    line per op: time-axis attention 992 seq x 801 tokens x 8 x 64, band-axis
+    attention 12816 seq x 62 tokens, STFT of 16 x 2 channels x 801 frames
+    (2048-point real FFTs; the bundled hop of 512), band split of 16 x 801
+    frames (the bundled 90-band layout).  Inputs are larger than L2."""
+    import torch
+
+    from karaoke_platform_sidecar_native_b200 import native
+
+    peaks = load_peaks()
+    p = native.Provider(0)
+    p.set_precision(True)
+    stream = torch.cuda.ExternalStream(p.stream)
+    g = torch.Generator(device="cuda").manual_seed(4)
+
+    def timed(fn, steps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        p.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    lines = []
+    d1, d2, d3 = 801, 62, 16
+    rows = d1 * d2 * d3
+    qkv = torch.randn(rows, 1536, device="cuda", generator=g).bfloat16()
+    gates = torch.rand(rows, 8, device="cuda", generator=g)
+    out = torch.empty(rows, 512, device="cuda", dtype=torch.bfloat16)
+    for name, pos, seqs, length in (("time-axis attention", 1, d2 * d3, d1), ("band-axis attention", 2, d1 * d3, d2)):
+        ms = timed(lambda: p.stage_attention(qkv, gates, out, d1, d2, d3, pos), max(5, args.steps))
+        flop = 4.0 * length * length * 64 * 8 * seqs
+        byts = rows * (1536 + 512) * 2 + rows * 8 * 4
+        line = {"op": f"{name}, {seqs} seq x {length} tokens x 8 heads x 64, bf16", "ms": round(ms, 4),
+                "tflops": round(flop / ms / 1e9, 1), "gbs": round(byts / ms / 1e6, 1),
+                "roofline": ({"bound": "tensor", "frac": round(flop / ms / 1e9 / peaks["tflops_burst"], 4),
+                              "peak_tflops": peaks["tflops_burst"]} if pos == 1 else
+                             {"bound": "hbm", "frac": round(byts / ms / 1e6 / peaks["hbm_gbs"], 4),
+                              "peak_gbs": peaks["hbm_gbs"]})}
+        lines.append(line)
+    del qkv, out, gates
+    frames = 801
+    length = (frames - 1) * 512
+    audio = torch.randn(16, 2, length, device="cuda", generator=g)
+    spec = torch.empty(16, frames, 1025, 2, 2, device="cuda")
+    ms = timed(lambda: p.stage_stft(audio, 16, length, spec), max(5, args.steps))
+    byts = audio.numel() * 4 + spec.numel() * 4
+    lines.append({"op": "STFT, 16 x 2 x 801 frames of 2048-point real FFT", "ms": round(ms, 4),
+                  "gbs": round(byts / ms / 1e6, 1),
+                  "roofline": {"bound": "hbm", "frac": round(byts / ms / 1e6 / peaks["hbm_gbs"], 4),
+                               "peak_gbs": peaks["hbm_gbs"]}})
+    x = torch.empty(16 * 90 * frames, 256, device="cuda")
+    p.load_model(modelpack.synthetic_pack(**modelpack.BENCH_RECIPE))
+    ms = timed(lambda: p.stage_band_split(spec, 16, frames, x), max(5, args.steps))
+    byts = spec.numel() * 4 + x.numel() * 4
+    lines.append({"op": "band split (RMSNorm + Linear per band), 16 x 801 frames, 90 bundled bands", "ms": round(ms, 4),
+                  "gbs": round(byts / ms / 1e6, 1),
+                  "roofline": {"bound": "hbm", "frac": round(byts / ms / 1e6 / peaks["hbm_gbs"], 4),
+                               "peak_gbs": peaks["hbm_gbs"]}})
+    for line in lines:
+        line.update({"config": "cfg4 op-level", "data": "synthetic N(0,1)", "dtype": "bf16"})
+        print(json.dumps(line), flush=True)
+    p.close()
     return 0
 
 

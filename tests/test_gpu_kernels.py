@@ -137,3 +137,45 @@ def test_istft_matches_oracle(provider, length):
     d_out = torch.zeros(1, 2, length, device="cuda")
     run(provider, provider.stage_istft, d_spec, d_mask, 1, length, d_out)
     assert snr_db(ref, d_out.cpu().numpy()[0]) > 100
+
+
+@pytest.fixture(scope="module")
+def provider_bf16():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    p = native.Provider(0)
+    p.set_precision(True)
+    yield p
+    p.close()
+
+
+@pytest.mark.parametrize("pos_dim", [1, 2])
+def test_attention_config4_shapes_bf16(provider_bf16, pos_dim):
+    # Config 4 op-level shapes, bf16 N(0,1) inputs: time axis 992 sequences x 801
+    # tokens (62 bands x 16 chunks), band axis 12816 sequences x 62 tokens.  The
+    # whole launch runs; 24 sequences are checked against an fp32 softmax of
+    # the same bf16 values (P is rounded to bf16 before P.V: 2^-8 relative).
+    d1, d2, d3 = 801, 62, 16
+    rows = d1 * d2 * d3
+    g = torch.Generator(device="cuda").manual_seed(4 + pos_dim)
+    qkv = torch.randn(rows, 1536, device="cuda", generator=g).bfloat16()
+    gates = torch.rand(rows, 8, device="cuda", generator=g)
+    out = torch.full((rows, 512), float("nan"), device="cuda", dtype=torch.bfloat16)
+    run(provider_bf16, provider_bf16.stage_attention, qkv, gates, out, d1, d2, d3, pos_dim)
+    assert torch.isfinite(out.float()).all()
+    x = qkv.view(d3, d2, d1, 1536)
+    o = out.view(d3, d2, d1, 512)
+    gt = gates.view(d3, d2, d1, 8)
+    idx = torch.Generator().manual_seed(9)
+    for _ in range(24):
+        c = int(torch.randint(d3, (1,), generator=idx))
+        if pos_dim == 1:
+            b = int(torch.randint(d2, (1,), generator=idx))
+            sel = (c, b, slice(None))
+        else:
+            f = int(torch.randint(d1, (1,), generator=idx))
+            sel = (c, slice(None), f)
+        ref = attention_reference(x[sel].contiguous(), gt[sel].contiguous(), x[sel].shape[0], 1, 1, 1)
+        got = o[sel].float()
+        assert rel_max(got, ref) < 3e-2
+        assert float((got - ref).abs().mean() / ref.abs().mean()) < 8e-3
