@@ -85,9 +85,12 @@ constexpr int kPolyPairs = 2;
 // running sum are rescaled -- otherwise P = exp2((s - m) c) <= 256 stays exact
 // enough in 16 bits and no O traffic is needed.
 //
-// The MMA warp runs its loop warp-uniform and issues each MMA under
-// elect.sync, with descriptors advanced by constant offsets.
-constexpr int kPairThreads = 320;
+// Two issuer warps run warp-uniform loops and issue each MMA under
+// elect.sync, with descriptors advanced by constant offsets: warp 1 issues
+// S = Q K^T as soon as a tile's S buffer is free, warp 10 issues O += P V as
+// soon as a tile's P is in TMEM, so neither waits behind the other's
+// dependencies; each commits its reads of a K/V stage to kv_empty (count 2).
+constexpr int kPairThreads = 352;   // warps: TMA, S issuer, 8 softmax, PV issuer
 constexpr float kRescaleLog2 = 8.0f;
 
 constexpr int kKvStages = 3;   // K/V ring depth: loads run two tiles ahead of the PV that frees a stage
@@ -149,7 +152,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* o_full = p_full + 2;                // [tile]
   uint64_t* o_empty = o_full + 2;               // [tile]
   uint64_t* drain = o_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (int i = 0; i < kKvStages; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);   // S issuer (K read) and PV issuer (V read)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -177,6 +180,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&o_empty[i], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(drain + 1, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -223,49 +227,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // MMA warp: warp-uniform control flow, one elected lane issues.  Step t =
-    // (unit, KV tile j) issues S(t) and then PV(t-1), which may belong to the
-    // previous unit.
+    // S issuer: warp-uniform, one elected lane issues S = Q K^T per tile as
+    // soon as the tile's S buffer is free, independent of the PV issuer.
     const uint32_t bf = ElemTraits<T>::kBf16;
-    const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
     const uint64_t q_desc = sw128_desc(smem_u32(sQ), 16, 1024);
     const uint64_t k_desc = sw128_desc(smem_u32(sK), 16, 1024);
-    const uint64_t v_desc = sw128_desc(smem_u32(sV), 8192, 1024);
     int sc[2] = {0, 0};   // S MMAs issued per tile
-    int pc[2] = {0, 0};   // PV MMAs issued per tile
-    int uc[2] = {0, 0};   // units whose O has been completed per tile
-    struct Pending {
-      bool valid;
-      int j, ntiles, st;
-    } prev = {false, 0, 0, 0};
-    auto issue_pv = [&](const Pending& pv) -> bool {
-      const int ksteps = min(kTile, round16(length - pv.j * kTile)) / 16;
-      const uint64_t vd = v_desc + static_cast<uint64_t>((pv.st * kQBytes) >> 4);
-      for (int x = 0; x < pv.ntiles; ++x) {
-        if (!mbar_wait_warp(&p_full[x], static_cast<uint32_t>(pc[x]) & 1u, abort_flag, args.err, kErrWaitMma))
-          return false;
-        // The first PV of a unit overwrites O: the previous unit's O must have been read.
-        if (pv.j == 0 && uc[x] > 0 &&
-            !mbar_wait_warp(&o_empty[x], static_cast<uint32_t>(uc[x] - 1) & 1u, abort_flag, args.err, kErrWaitMma))
-          return false;
-        tc_fence_after();
-        if (elect_one()) {
-          const uint32_t o_col = tmem_base + kColO + x * kDimHead;
-          const uint32_t p_col = tmem_base + kColP + x * (kTile / 2);
-#pragma unroll
-          for (int kk = 0; kk < kTile / 16; ++kk)
-            if (kk < ksteps)
-              umma_f16_ts(o_col, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o, (pv.j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&o_full[x]);
-        }
-        __syncwarp();
-        ++pc[x];
-        if (pv.j == nkv - 1) ++uc[x];
-      }
-      if (elect_one()) umma_commit(&kv_empty[pv.st]);
-      __syncwarp();
-      return true;
-    };
     bool ok = true;
     int kvc = 0;
     for (int lu = 0; ok && lu < n_local; ++lu) {
@@ -303,17 +270,63 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           __syncwarp();
           ++sc[x];
         }
-        if (ok && prev.valid && !issue_pv(prev)) ok = false;
-        prev.valid = true;
-        prev.j = j;
-        prev.ntiles = pu.ntiles;
-        prev.st = st;
+        if (ok && elect_one()) umma_commit(&kv_empty[st]);   // K of this stage read
+        __syncwarp();
       }
     }
-    if (ok && prev.valid) issue_pv(prev);
     if (elect_one()) {
       umma_commit(drain);
       wait_drain(drain, 0, args.err);
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // PV issuer: O_x += P_x V as soon as tile x's P is in TMEM.
+    const uint32_t bf = ElemTraits<T>::kBf16;
+    const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
+    const uint64_t v_desc = sw128_desc(smem_u32(sV), 8192, 1024);
+    int pc[2] = {0, 0};   // PV MMAs issued per tile
+    int uc[2] = {0, 0};   // units whose O has been completed per tile
+    bool ok = true;
+    int kvc = 0;
+    for (int lu = 0; ok && lu < n_local; ++lu) {
+      const PairUnit pu = pair_unit(args, unit_of(lu));
+      for (int j = 0; ok && j < nkv; ++j, ++kvc) {
+        const int st = kvc % kKvStages;
+        const int ksteps = min(kTile, round16(length - j * kTile)) / 16;
+        const uint64_t vd = v_desc + static_cast<uint64_t>((st * kQBytes) >> 4);
+        for (int x = 0; x < pu.ntiles && ok; ++x) {
+          if (!mbar_wait_warp(&p_full[x], static_cast<uint32_t>(pc[x]) & 1u, abort_flag, args.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          // The first PV of a unit overwrites O: the previous unit's O must have been read.
+          if (j == 0 && uc[x] > 0 &&
+              !mbar_wait_warp(&o_empty[x], static_cast<uint32_t>(uc[x] - 1) & 1u, abort_flag, args.err,
+                              kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t o_col = tmem_base + kColO + x * kDimHead;
+            const uint32_t p_col = tmem_base + kColP + x * (kTile / 2);
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk)
+              if (kk < ksteps)
+                umma_f16_ts(o_col, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&o_full[x]);
+          }
+          __syncwarp();
+          ++pc[x];
+          if (j == nkv - 1) ++uc[x];
+        }
+        if (ok && elect_one()) umma_commit(&kv_empty[st]);   // V of this stage read
+        __syncwarp();
+      }
+    }
+    if (elect_one()) {
+      umma_commit(drain + 1);
+      wait_drain(drain + 1, 0, args.err);
     }
     __syncwarp();
   } else {
