@@ -42,6 +42,14 @@ int vocalarc_b200_separate(native_gpu *gpu, const float *audio, int length, floa
 int vocalarc_b200_separate_chunked(native_gpu *gpu, const float *audio, int length,
                                    int chunk_samples, int model_batch, float *vocals);
 
+/* The ONNX sidecar's quality pass (Separator::separate, onnx/native/onnx_sidecar.cpp:556-575;
+   bigshift :784-790): the chunked forward of `bigshifts` circularly rotated copies of the
+   mix (shift = length / bigshifts), each rotated back and averaged; with tta != 0 also of
+   the channel-swapped and the polarity-flipped mix, combined as the reference does,
+   ((v + swapped back) - (-(flipped))) / 3.  All copies run as one batch on the device. */
+int vocalarc_b200_separate_tta(native_gpu *gpu, const float *audio, int length, int chunk_samples,
+                               int model_batch, int bigshifts, int tta, float *vocals);
+
 /* Device-pointer variants on the provider's stream; they return after
    enqueueing (call vocalarc_b200_synchronize).  `tracks` planar clips of
    `length` samples each are laid out back to back ([tracks][2][length]). */

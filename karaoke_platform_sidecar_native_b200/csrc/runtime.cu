@@ -214,6 +214,10 @@ struct native_gpu {
   float* seam_in = nullptr;     // the previous range's seam, copied here
   long long seam_cap = 0;       // floats allocated in each seam buffer
   int has_seam_in = 0;
+  // bigshift + TTA variant tracks and their estimates (vocalarc_b200_separate_tta)
+  long long ws_tta = 0;
+  float* tta_in = nullptr;
+  float* tta_out = nullptr;
   // launch trace: one event after every launch on the provider stream
   long long launches = 0;
   int trace = 0;
@@ -859,7 +863,7 @@ void native_gpu_destroy(native_gpu* g) {
   if (g->stream != nullptr) cudaStreamSynchronize(g->stream);
   void* ptrs[] = {g->x, g->x_alt, g->x16, g->row_inv, g->qkv, g->attn, g->gates, g->spec, g->mask, g->frames_buf,
                   g->seg_out, g->audio_in, g->audio_out, g->d_tiles1, g->d_tiles2, g->d_err, g->d_window,
-                  g->d_twiddle, g->d_rope, g->abi_mask_mem, g->seam_out, g->seam_in};
+                  g->d_twiddle, g->d_rope, g->abi_mask_mem, g->seam_out, g->seam_in, g->tta_in, g->tta_out};
   for (void* p : ptrs)
     if (p != nullptr) cudaFree(p);
   for (auto& e : g->block_cache) cudaFree(e.mem);
@@ -1298,6 +1302,36 @@ int vocalarc_b200_range_finish(native_gpu* g, float* d_vocals) {
   if (!launched(g, launch_demix_range(g->seg_out, dm, g->range_chunks, g->range_batch, r, g->stream), "demix range"))
     return 0;
   return sync_and_check(g, "range finish") ? 1 : 0;
+}
+
+int vocalarc_b200_separate_tta(native_gpu* g, const float* audio, int length, int chunk_samples, int model_batch,
+                               int bigshifts, int tta, float* vocals) {
+  if (!active(g) || audio == nullptr || vocals == nullptr || length <= 0) return 0;
+  cudaSetDevice(g->device);
+  const int shifts = bigshifts < 1 ? 1 : bigshifts;
+  const int variants = tta ? 3 : 1;
+  const long long n2 = 2ll * length;
+  const long long total = n2 * shifts * variants;
+  if (!ensure_audio(g, n2)) return 0;
+  if (total > g->ws_tta) {
+    g->ws_tta = 0;
+    if (!grow(g, &g->tta_in, static_cast<size_t>(total) * 4, "cudaMalloc(tta_in)") ||
+        !grow(g, &g->tta_out, static_cast<size_t>(total) * 4, "cudaMalloc(tta_out)"))
+      return 0;
+    g->ws_tta = total;
+  }
+  if (!cuda_ok(g, cudaMemcpyAsync(g->audio_in, audio, n2 * 4, cudaMemcpyHostToDevice, g->stream), "H2D audio")) return 0;
+  if (!launched(g, launch_tta_inputs(g->audio_in, length, shifts, variants, g->tta_in, g->stream), "tta inputs"))
+    return 0;
+  // All shifted / swapped / inverted copies go through the chunked forward as
+  // one batch of tracks.
+  if (!separate_device_impl(g, g->tta_in, shifts * variants, length, 1, chunk_samples, model_batch, g->tta_out))
+    return 0;
+  if (!launched(g, launch_tta_combine(g->tta_out, length, shifts, tta ? 1 : 0, g->audio_out, g->stream), "tta combine"))
+    return 0;
+  if (!cuda_ok(g, cudaMemcpyAsync(vocals, g->audio_out, n2 * 4, cudaMemcpyDeviceToHost, g->stream), "D2H vocals"))
+    return 0;
+  return sync_and_check(g, "separate_tta") ? 1 : 0;
 }
 
 int vocalarc_b200_synchronize(native_gpu* g) {

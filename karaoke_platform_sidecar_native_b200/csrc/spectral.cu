@@ -383,6 +383,57 @@ __global__ void __launch_bounds__(256) demix_range_kernel(const float* __restric
   }
 }
 
+// ---------------------------------------------------------------- bigshifts + TTA
+// Separator::separate / bigshift of the ONNX sidecar (onnx_sidecar.cpp:556-575,
+// :784-790, rotate/unrotate/scale/add :385-421).  Variant v of the mix (0: as
+// is, 1: channels swapped, 2: polarity flipped) rotated by shift k of B:
+// out[v][k][ch][i] = sign_v * mix[ch_v][(n - shift_k + i) % n].
+__global__ void __launch_bounds__(256) tta_inputs_kernel(const float* __restrict__ mix, int n, int shifts,
+                                                         int variants, float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int vk = blockIdx.y;   // v * shifts + k
+  const int v = vk / shifts, k = vk - v * shifts;
+  const int shift = static_cast<int>((static_cast<long long>(k) * (n / shifts)) % n);
+  const int src = static_cast<int>((static_cast<long long>(n) - shift + i) % n);
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch) {
+    const int ch_src = v == 1 ? 1 - ch : ch;
+    float x = mix[static_cast<long long>(ch_src) * n + src];
+    if (v == 2) x *= -1.0f;
+    out[(static_cast<long long>(vk) * 2 + ch) * n + i] = x;
+  }
+}
+
+// Combines the estimates est[v][k][2][n] in the reference's float order:
+// bigshift r_v = (0 + e_0 + e_1 + ...) * (1/B) with e_k rotated back; without
+// TTA the result is r_0, with TTA ((r_0 + swap(r_1)) + (-1) * (-1 * r_2)) * (1/3).
+__global__ void __launch_bounds__(256) tta_combine_kernel(const float* __restrict__ est, int n, int shifts,
+                                                          int tta, float* __restrict__ vocals) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int ch = blockIdx.y;
+  const float inv_shifts = 1.0f / static_cast<float>(shifts);
+  float r[3];
+  for (int v = 0; v < (tta ? 3 : 1); ++v) {
+    const int ch_v = v == 1 ? 1 - ch : ch;   // the swapped estimate is swapped back
+    float acc = 0.0f;
+    for (int k = 0; k < shifts; ++k) {
+      const int shift = static_cast<int>((static_cast<long long>(k) * (n / shifts)) % n);
+      const int src = static_cast<int>((static_cast<long long>(i) + shift) % n);
+      acc = __fadd_rn(acc, est[((static_cast<long long>(v) * shifts + k) * 2 + ch_v) * n + src]);
+    }
+    r[v] = __fmul_rn(acc, inv_shifts);
+  }
+  float out = r[0];
+  if (tta) {
+    const float inverted = __fmul_rn(r[2], -1.0f);
+    const float total = __fadd_rn(r[0], r[1]);
+    out = __fmul_rn(__fadd_rn(total, __fmul_rn(-1.0f, inverted)), 1.0f / 3.0f);
+  }
+  vocals[static_cast<long long>(ch) * n + i] = out;
+}
+
 }  // namespace
 
 cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int frames, const float* window,
@@ -448,6 +499,18 @@ cudaError_t launch_demix_range(const float* seg_out, SegmentMap map, int chunks,
                                const DemixRange& range, cudaStream_t stream) {
   if (range.p1 <= range.p0) return cudaSuccess;
   demix_range_kernel<<<(range.p1 - range.p0 + 255) / 256, 256, 0, stream>>>(seg_out, map, chunks, model_batch, range);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tta_inputs(const float* mix, int n, int shifts, int variants, float* out, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  tta_inputs_kernel<<<dim3((n + 255) / 256, shifts * variants), 256, 0, stream>>>(mix, n, shifts, variants, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tta_combine(const float* est, int n, int shifts, int tta, float* vocals, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  tta_combine_kernel<<<dim3((n + 255) / 256, 2), 256, 0, stream>>>(est, n, shifts, tta, vocals);
   return cudaGetLastError();
 }
 

@@ -153,6 +153,10 @@ struct DemixRange {
 };
 cudaError_t launch_demix_range(const float* seg_out, SegmentMap map, int chunks, int model_batch,
                                const DemixRange& range, cudaStream_t stream);
+// Bigshift + TTA variants of a mix ([variants][shifts][2][n]) and the
+// reference-order combination of their estimates into vocals [2][n].
+cudaError_t launch_tta_inputs(const float* mix, int n, int shifts, int variants, float* out, cudaStream_t stream);
+cudaError_t launch_tta_combine(const float* est, int n, int shifts, int tta, float* vocals, cudaStream_t stream);
 cudaError_t launch_transpose_tokens(const float* src, float* dst, int s0, int l0, cudaStream_t stream);
 cudaError_t upload_band_tables(const int* first, const int* dims);
 

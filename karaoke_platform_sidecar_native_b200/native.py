@@ -73,6 +73,8 @@ _SIGNATURES = {
     "vocalarc_b200_trace_end": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int]),
     "vocalarc_b200_stage_gemm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int,
                                                 ctypes.c_int, _vp, _vp]),
+    "vocalarc_b200_separate_tta": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_int, _vp]),
     "vocalarc_b200_chunk_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _ip, _ip, _ip, _ip]),
     "vocalarc_b200_range_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                    ctypes.c_int]),
@@ -196,6 +198,15 @@ class Provider:
         out = np.zeros_like(audio)
         self.check(self.lib.vocalarc_b200_separate_chunked(self.handle, fptr(audio), audio.shape[1], chunk,
                                                            model_batch, fptr(out)), "separate_chunked")
+        return out
+
+    def separate_tta(self, audio: np.ndarray, bigshifts: int = 2, tta: bool = True, chunk: int = 0,
+                     model_batch: int = 1) -> np.ndarray:
+        """The ONNX sidecar's bigshift + TTA pass over the chunked forward."""
+        audio = np.ascontiguousarray(audio, dtype=np.float32)
+        out = np.zeros_like(audio)
+        self.check(self.lib.vocalarc_b200_separate_tta(self.handle, fptr(audio), audio.shape[1], chunk, model_batch,
+                                                       bigshifts, 1 if tta else 0, fptr(out)), "separate_tta")
         return out
 
     def separate_device(self, d_audio, tracks: int, length: int, d_vocals, chunked: bool = False, chunk: int = 0,

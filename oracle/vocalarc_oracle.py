@@ -353,3 +353,54 @@ def demix(predict, mix: np.ndarray, chunk: int = CHUNK_SAMPLES, batch: int = 1) 
     if padded != length:
         output = output[:, border:border + length]
     return output
+
+
+# ---------------------------------------------------------------- bigshifts + TTA
+def rotate_audio(audio: np.ndarray, shift: int) -> np.ndarray:
+    """``rotate_audio`` (onnx_sidecar.cpp:385-396): out[i] = in[(n - shift + i) % n]."""
+    n = audio.shape[1]
+    if n == 0:
+        return audio.copy()
+    shift %= n
+    return audio[:, (n - shift + np.arange(n)) % n].astype(F32)
+
+
+def unrotate_audio(audio: np.ndarray, shift: int) -> np.ndarray:
+    """``unrotate_audio`` (onnx_sidecar.cpp:398-408): out[i] = in[(i + shift) % n]."""
+    n = audio.shape[1]
+    if n == 0:
+        return audio.copy()
+    shift %= n
+    return audio[:, (np.arange(n) + shift) % n].astype(F32)
+
+
+def bigshift(separate, mix: np.ndarray, count: int) -> np.ndarray:
+    """``bigshift`` (onnx_sidecar.cpp:784-790): the mean of ``count`` chunked
+    separations of circularly rotated copies, each rotated back.  Float32
+    arithmetic in the reference's order: result = 0; result += 1 * estimate_k
+    (k ascending); result *= 1/count."""
+    mix = np.asarray(mix, dtype=F32)
+    result = np.zeros_like(mix)
+    shift_size = mix.shape[1] // count
+    for index in range(count):
+        estimate = unrotate_audio(separate(rotate_audio(mix, index * shift_size)), index * shift_size)
+        result = (result + F32(1.0) * estimate).astype(F32)
+    return (result * F32(1.0 / count)).astype(F32)
+
+
+def separate_tta(separate, mix: np.ndarray, bigshifts: int = 2, tta: bool = True) -> np.ndarray:
+    """``Separator::separate`` (onnx_sidecar.cpp:556-575).  With TTA the estimate
+    of the channel-swapped mix (swapped back) is added and the polarity-flipped
+    estimate ``inverted = -bigshift(-mix)`` is combined with ``right_scale = -1``
+    (:572-573), then scaled by 1/3 -- restated exactly as the reference computes
+    it."""
+    mix = np.asarray(mix, dtype=F32)
+    bigshifts = max(1, int(bigshifts))
+    vocals = bigshift(separate, mix, bigshifts)
+    if not tta:
+        return vocals
+    restored = bigshift(separate, mix[::-1].copy(), bigshifts)[::-1].copy()
+    inverted = (bigshift(separate, (mix * F32(-1.0)).astype(F32), bigshifts) * F32(-1.0)).astype(F32)
+    total = (vocals + F32(1.0) * restored).astype(F32)
+    total = (total + F32(-1.0) * inverted).astype(F32)
+    return (total * F32(1.0 / 3.0)).astype(F32)
