@@ -1,8 +1,9 @@
 // Spectral front/back end and memory-bound kernels of the separation forward.
 //
 //  * stft_kernel: center=True framing with reflect padding, periodic Hann
-//    window, 2048-point real FFT through a 1024-point complex FFT in shared
-//    memory (stft_channels, native/vocalarc_separation.c:1044-1064).  The
+//    window, 2048-point real FFT through a 1024-point complex FFT done as a
+//    four-step 32 x 32 transform in registers, one warp per frame and channel
+//    (stft_channels, native/vocalarc_separation.c:1044-1064).  The
 //    reference FFT runs in double on the host; this one is fp32 with
 //    double-precision twiddles, checked against the oracle by SNR.
 //  * band_split_kernel: per band gather + RMSNorm + Linear(d_b -> 256) + bias
@@ -55,66 +56,132 @@ __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
-// Two in-place 1024-point radix-2 decimation-in-frequency FFTs (forward,
-// e^{-2 pi i k n / 1024}); the result lands in bit-reversed order.
-// tw[k] = e^{-2 pi i k / 2048}, so the 1024-point twiddle W^k is tw[2k].
-__device__ void fft1024_pair(float2* buf0, float2* buf1, const float2* tw) {
-  for (int span = 512, log_span = 9; span >= 1; span >>= 1, --log_span) {
-    for (int b = threadIdx.x; b < 1024; b += blockDim.x) {
-      float2* buf = b < 512 ? buf0 : buf1;
-      const int bb = b & 511;
-      const int pos = bb & (span - 1);
-      const int i = ((bb >> log_span) << (log_span + 1)) + pos;
-      const int j = i + span;
-      const float2 a = buf[i];
-      const float2 c = buf[j];
-      buf[i] = make_float2(a.x + c.x, a.y + c.y);
-      const float2 w = tw[(pos << (9 - log_span)) * 2];
-      buf[j] = cmul(make_float2(a.x - c.x, a.y - c.y), w);
+
+// ---------------------------------------------------------------- STFT
+// One warp per (frame, channel), four frames per CTA.  The 2048-point real FFT
+// is a 1024-point complex FFT of z[n] = x[2n] + i x[2n+1] done as a four-step
+// 32 x 32 transform with n = 32 n1 + n2, k = k1 + 32 k2: lane n2 holds
+// z[32 n1 + n2] for all n1 in registers, runs a 32-point FFT over n1, applies
+// W_1024^(n2 k1), the warp transposes through shared memory, and lane k1 runs
+// the second 32-point FFT over n2, giving Z[k1 + 32 k2].  Then
+// X[k] = E[k] + W_2048^k O[k] from Z[k] and Z[1024 - k].  tw[k] = e^{-2 pi i k / 2048}.
+constexpr int kStftFramesPerCta = 4;
+constexpr int kStftTw = 1028;   // twiddle table entries kept in shared memory (1025 used)
+constexpr int kStftBuf = 32 * 33;   // one warp's padded 32 x 32 transpose buffer (float2)
+constexpr int kStftSmem = (kStftTw + 2 * kStftFramesPerCta * kStftBuf) * 8;
+
+__host__ __device__ constexpr int brev5(int i) {
+  return ((i & 1) << 4) | ((i & 2) << 2) | (i & 4) | ((i & 8) >> 2) | ((i & 16) >> 4);
+}
+
+// e^{-2 pi i k / 2048} for 0 <= k < 2048 from the half table.
+__device__ __forceinline__ float2 tw2048(const float2* tw, int k) {
+  const float2 w = tw[k <= 1024 ? k : k - 1024];
+  return k <= 1024 ? w : make_float2(-w.x, -w.y);
+}
+
+// One radix-2 decimation-in-time stage of span M over 32 registers.
+template <int M>
+__device__ __forceinline__ void fft32_stage(float2 (&b)[32], const float2* tw) {
+  constexpr int kHalf = M / 2;
+#pragma unroll
+  for (int k = 0; k < 32; k += M) {
+#pragma unroll
+    for (int j = 0; j < kHalf; ++j) {
+      const float2 u = b[k + j];
+      float2 t = b[k + j + kHalf];
+      if (j != 0) t = cmul(t, tw[64 * j * (32 / M)]);
+      b[k + j] = make_float2(u.x + t.x, u.y + t.y);
+      b[k + j + kHalf] = make_float2(u.x - t.x, u.y - t.y);
     }
-    __syncthreads();
   }
 }
 
-__device__ __forceinline__ int brev10(int x) { return static_cast<int>(__brev(static_cast<unsigned>(x)) >> 22); }
+// In-register radix-2 decimation-in-time 32-point FFT (forward), natural
+// order in and out; every index is a compile-time constant.
+__device__ __forceinline__ void fft32(float2 (&a)[32], const float2* tw) {
+  float2 b[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) b[i] = a[brev5(i)];
+  fft32_stage<2>(b, tw);
+  fft32_stage<4>(b, tw);
+  fft32_stage<8>(b, tw);
+  fft32_stage<16>(b, tw);
+  fft32_stage<32>(b, tw);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) a[i] = b[i];
+}
 
-__global__ void __launch_bounds__(256) stft_kernel(const float* __restrict__ audio, SegmentMap map, int frames,
+__global__ void __launch_bounds__(256, 3) stft_kernel(const float* __restrict__ audio, SegmentMap map, int frames,
                                                    const float* __restrict__ window,
                                                    const float2* __restrict__ twiddle, float* __restrict__ spec) {
-  __shared__ float2 buf[2][1024];
-  __shared__ float2 tw[1025];
-  const int f = blockIdx.x;
-  const int c = blockIdx.y;
+  extern __shared__ float2 stft_smem[];
+  float2* tw = stft_smem;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float2* buf = stft_smem + kStftTw + warp * kStftBuf;
   for (int k = threadIdx.x; k < 1025; k += blockDim.x) tw[k] = twiddle[k];
+  const int f = blockIdx.x * kStftFramesPerCta + (warp >> 1);
+  const int ch = warp & 1;
+  const int c = blockIdx.y;
+  const bool active = f < frames;   // warp-uniform; inactive warps only help load the table
   const int start = f * kHop - kNfft / 2;
-  for (int n = threadIdx.x; n < kNfft; n += blockDim.x) {
-    const int s = reflect_index(start + n, map.seg_length);
-    const float w = window[n];
-#pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-      const float x = segment_sample(audio, map, c, ch, s) * w;
-      float* slot = reinterpret_cast<float*>(&buf[ch][n >> 1]);
-      slot[n & 1] = x;
+  // Contiguous source run for frames that need no reflection (warp-uniform).
+  long long base = -1;
+  if (active && start >= 0 && start + kNfft <= map.seg_length) {
+    if (map.mode == 0) {
+      base = c * map.clip_stride + static_cast<long long>(ch) * map.clip_length + start;
+    } else {
+      const int cs = (map.first_chunk + c) * map.step;
+      const int available = cs < map.padded ? min(map.seg_length, map.padded - cs) : 0;
+      if (start + kNfft <= available) {
+        const int j0 = cs + start - map.border;
+        if (j0 >= 0 && j0 + kNfft <= map.clip_length) base = static_cast<long long>(ch) * map.clip_length + j0;
+      }
     }
   }
-  __syncthreads();
-  fft1024_pair(buf[0], buf[1], tw);
-  // X[k] = E[k] + W^k O[k],  E = (Z[k] + conj Z[1024-k]) / 2,  O = (Z[k] - conj Z[1024-k]) / (2i).
-  float4* out = reinterpret_cast<float4*>(spec) + (static_cast<long long>(c) * frames + f) * kFreqBins;
-  for (int k = threadIdx.x; k < kFreqBins; k += blockDim.x) {
-    float v[4];
-    const float2 w = tw[k];
+  float2 a[32];
 #pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-      const float2 zk = buf[ch][brev10(k & 1023)];
-      const float2 zr = buf[ch][brev10((1024 - k) & 1023)];
-      const float2 e = make_float2(0.5f * (zk.x + zr.x), 0.5f * (zk.y - zr.y));
-      const float2 o = make_float2(0.5f * (zk.y + zr.y), -0.5f * (zk.x - zr.x));
-      const float2 x = make_float2(e.x + (w.x * o.x - w.y * o.y), e.y + (w.x * o.y + w.y * o.x));
-      v[2 * ch] = x.x;
-      v[2 * ch + 1] = x.y;
+  for (int n1 = 0; n1 < 32; ++n1) {
+    const int n = 64 * n1 + 2 * lane;
+    const float2 w = *reinterpret_cast<const float2*>(window + n);
+    float x0 = 0.f, x1 = 0.f;
+    if (!active) {
+    } else if (base >= 0) {
+      x0 = __ldg(audio + base + n);
+      x1 = __ldg(audio + base + n + 1);
+    } else {
+      x0 = segment_sample(audio, map, c, ch, reflect_index(start + n, map.seg_length));
+      x1 = segment_sample(audio, map, c, ch, reflect_index(start + n + 1, map.seg_length));
     }
-    out[k] = make_float4(v[0], v[1], v[2], v[3]);
+    a[n1] = make_float2(x0 * w.x, x1 * w.y);
+  }
+  // The sample loads above are in flight while the table copy completes.
+  __syncthreads();
+  if (!active) return;
+  fft32(a, tw);   // a[k1] for this n2 = lane
+#pragma unroll
+  for (int k1 = 1; k1 < 32; ++k1) a[k1] = cmul(a[k1], tw2048(tw, 2 * ((lane * k1) & 1023)));
+#pragma unroll
+  for (int k1 = 0; k1 < 32; ++k1) buf[k1 * 33 + lane] = a[k1];
+  __syncwarp();
+#pragma unroll
+  for (int n2 = 0; n2 < 32; ++n2) a[n2] = buf[lane * 33 + n2];
+  __syncwarp();
+  fft32(a, tw);   // a[k2] = Z[lane + 32 k2]
+#pragma unroll
+  for (int k2 = 0; k2 < 32; ++k2) buf[k2 * 33 + lane] = a[k2];
+  __syncwarp();
+  // X[k] = E[k] + W^k O[k],  E = (Z[k] + conj Z[1024-k]) / 2,  O = (Z[k] - conj Z[1024-k]) / (2i).
+  float* out = spec + (static_cast<long long>(c) * frames + f) * kFreqBins * 4 + 2 * ch;
+  for (int k = lane; k < kFreqBins; k += 32) {
+    const int kk = k & 1023, kr = (1024 - k) & 1023;
+    const float2 zk = buf[(kk >> 5) * 33 + (kk & 31)];
+    const float2 zr = buf[(kr >> 5) * 33 + (kr & 31)];
+    const float2 w = tw[k];
+    const float2 e = make_float2(0.5f * (zk.x + zr.x), 0.5f * (zk.y - zr.y));
+    const float2 o = make_float2(0.5f * (zk.y + zr.y), -0.5f * (zk.x - zr.x));
+    *reinterpret_cast<float2*>(out + static_cast<long long>(k) * 4) =
+        make_float2(e.x + (w.x * o.x - w.y * o.y), e.y + (w.x * o.y + w.y * o.x));
   }
 }
 
@@ -211,59 +278,69 @@ __global__ void __launch_bounds__(256) row_stats_kernel(const float* __restrict_
 }
 
 // ---------------------------------------------------------------- iSTFT
-__global__ void __launch_bounds__(256) istft_frames_kernel(const float* __restrict__ spec,
-                                                           const float* __restrict__ mask, int frames,
-                                                           const float* __restrict__ window,
-                                                           const float2* __restrict__ twiddle,
-                                                           float* __restrict__ frames_out) {
-  __shared__ float2 y[2][kFreqBins];
-  __shared__ float2 buf[2][1024];
-  __shared__ float2 tw[1025];
-  const int f = blockIdx.x;
-  const int c = blockIdx.y;
+// Inverse of the STFT frame transform, one warp per (frame, channel), four
+// frames per CTA.  Y = spec * mask (complex); the 2048-point inverse real FFT is
+// a 1024-point complex FFT of Z[k] = (Y[k] + conj Y[1024-k]) +
+// i e^{+2 pi i k / 2048} (Y[k] - conj Y[1024-k]): lane n2 gathers conj(Z) at
+// k = 32 n1 + n2, the four-step forward FFT of stft_kernel runs, and the
+// conjugate of the result, / 2048 and windowed, is the frame:
+// x[2m] + i x[2m+1] = conj(FFT(conj Z))[m] / 2048.  The imaginary parts of
+// Y[0] and Y[1024] do not reach the real inverse and are dropped.
+__global__ void __launch_bounds__(256, 3) istft_frames_kernel(const float* __restrict__ spec,
+                                                              const float* __restrict__ mask, int frames,
+                                                              const float* __restrict__ window,
+                                                              const float2* __restrict__ twiddle,
+                                                              float* __restrict__ frames_out) {
+  extern __shared__ float2 stft_smem[];
+  float2* tw = stft_smem;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float2* buf = stft_smem + kStftTw + warp * kStftBuf;
   for (int k = threadIdx.x; k < 1025; k += blockDim.x) tw[k] = twiddle[k];
-  const long long base = (static_cast<long long>(c) * frames + f) * kFreqBins;
-  const float4* s4 = reinterpret_cast<const float4*>(spec) + base;
-  const float4* m4 = reinterpret_cast<const float4*>(mask) + base;
-  for (int k = threadIdx.x; k < kFreqBins; k += blockDim.x) {
-    const float4 s = s4[k];
-    const float4 m = m4[k];
-    float2 y0 = make_float2(s.x * m.x - s.y * m.y, s.x * m.y + s.y * m.x);
-    float2 y1 = make_float2(s.z * m.z - s.w * m.w, s.z * m.w + s.w * m.z);
-    if (k == 0 || k == 1024) {  // the real part of the inverse ignores these imaginary parts
-      y0.y = 0.f;
-      y1.y = 0.f;
-    }
-    y[0][k] = y0;
-    y[1][k] = y1;
-  }
-  __syncthreads();
-  // Z[k] = (X[k] + conj X[1024-k]) + i e^{+2 pi i k / 2048} (X[k] - conj X[1024-k]); store conj(Z)
-  // so that a forward FFT followed by conjugation gives the inverse.
-  for (int k = threadIdx.x; k < 1024; k += blockDim.x) {
-    const float2 e = make_float2(tw[k].x, -tw[k].y);
+  const int f = blockIdx.x * kStftFramesPerCta + (warp >> 1);
+  const int ch = warp & 1;
+  const int c = blockIdx.y;
+  const bool active = f < frames;   // warp-uniform
+  const long long base = ((static_cast<long long>(c) * frames + (active ? f : 0)) * kFreqBins) * 4 + 2 * ch;
+  auto bin = [&](int k) {   // Y[k] of this channel
+    const float2 sv = *reinterpret_cast<const float2*>(spec + base + 4ll * k);
+    const float2 mv = *reinterpret_cast<const float2*>(mask + base + 4ll * k);
+    float2 y = make_float2(sv.x * mv.x - sv.y * mv.y, sv.x * mv.y + sv.y * mv.x);
+    if (k == 0 || k == 1024) y.y = 0.f;
+    return y;
+  };
+  float2 a[32];
 #pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-      const float2 a = y[ch][k];
-      const float2 b = y[ch][1024 - k];
-      const float2 sum = make_float2(a.x + b.x, a.y - b.y);
-      const float2 dif = make_float2(a.x - b.x, a.y + b.y);
+  for (int n1 = 0; n1 < 32; ++n1) {
+    const int k = 32 * n1 + lane;
+    a[n1] = make_float2(0.f, 0.f);
+    if (active) {
+      const float2 ya = bin(k), yb = bin(1024 - k);
+      const float2 t = __ldg(twiddle + k);
+      const float2 e = make_float2(t.x, -t.y);
+      const float2 sum = make_float2(ya.x + yb.x, ya.y - yb.y);
+      const float2 dif = make_float2(ya.x - yb.x, ya.y + yb.y);
       const float2 ed = cmul(e, dif);
-      const float2 z = make_float2(sum.x - ed.y, sum.y + ed.x);
-      buf[ch][k] = make_float2(z.x, -z.y);
+      a[n1] = make_float2(sum.x - ed.y, -(sum.y + ed.x));   // conj(Z[k])
     }
   }
-  __syncthreads();
-  fft1024_pair(buf[0], buf[1], tw);
-  const float scale = 1.0f / 2048.0f;
-  for (int m = threadIdx.x; m < 1024; m += blockDim.x) {
-    const float w0 = window[2 * m], w1 = window[2 * m + 1];
+  __syncthreads();   // twiddle table in shared memory ready
+  if (!active) return;
+  fft32(a, tw);
 #pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-      const float2 z = buf[ch][brev10(m)];
-      float2* dst = reinterpret_cast<float2*>(frames_out + ((static_cast<long long>(c) * 2 + ch) * frames + f) * kNfft);
-      dst[m] = make_float2(z.x * scale * w0, -z.y * scale * w1);
-    }
+  for (int k1 = 1; k1 < 32; ++k1) a[k1] = cmul(a[k1], tw2048(tw, 2 * ((lane * k1) & 1023)));
+#pragma unroll
+  for (int k1 = 0; k1 < 32; ++k1) buf[k1 * 33 + lane] = a[k1];
+  __syncwarp();
+#pragma unroll
+  for (int n2 = 0; n2 < 32; ++n2) a[n2] = buf[lane * 33 + n2];
+  fft32(a, tw);   // a[k2] = FFT(conj Z)[lane + 32 k2]
+  const float scale = 1.0f / 2048.0f;
+  float2* dst = reinterpret_cast<float2*>(frames_out + ((static_cast<long long>(c) * 2 + ch) * frames + f) * kNfft);
+#pragma unroll
+  for (int k2 = 0; k2 < 32; ++k2) {
+    const int m = lane + 32 * k2;
+    const float2 w = *reinterpret_cast<const float2*>(window + 2 * m);
+    dst[m] = make_float2(a[k2].x * scale * w.x, -a[k2].y * scale * w.y);
   }
 }
 
@@ -439,7 +516,14 @@ __global__ void __launch_bounds__(256) tta_combine_kernel(const float* __restric
 cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int frames, const float* window,
                         const float2* twiddle, float* spec, cudaStream_t stream) {
   if (segments <= 0 || frames <= 0) return cudaSuccess;
-  stft_kernel<<<dim3(frames, segments), 256, 0, stream>>>(audio, map, frames, window, twiddle, spec);
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(stft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStftSmem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  stft_kernel<<<dim3((frames + kStftFramesPerCta - 1) / kStftFramesPerCta, segments), 256, kStftSmem, stream>>>(
+      audio, map, frames, window, twiddle, spec);
   return cudaGetLastError();
 }
 
@@ -475,7 +559,15 @@ cudaError_t launch_row_stats(const float* x, long long rows, void* x16, float* i
 cudaError_t launch_istft_frames(const float* spec, const float* mask, int segments, int frames, const float* window,
                                 const float2* twiddle, float* frames_out, cudaStream_t stream) {
   if (segments <= 0 || frames <= 0) return cudaSuccess;
-  istft_frames_kernel<<<dim3(frames, segments), 256, 0, stream>>>(spec, mask, frames, window, twiddle, frames_out);
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(istft_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStftSmem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  istft_frames_kernel<<<dim3((frames + kStftFramesPerCta - 1) / kStftFramesPerCta, segments), 256, kStftSmem,
+                        stream>>>(spec, mask, frames, window, twiddle, frames_out);
   return cudaGetLastError();
 }
 
