@@ -548,7 +548,7 @@ cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, int sm_cou
 // warp whose 32 rows all lie at or past the sequence length (rows 96-127 for
 // L = 90) does no softmax or output work: the rows of P it leaves stale only
 // reach rows of O that are never stored.
-constexpr int kItemThreads = 320;
+constexpr int kItemThreads = 352;   // warps: TMA, S issuer, 8 softmax, PV issuer
 constexpr int kItemStages = 4;
 
 struct ItemSmem {
@@ -584,7 +584,7 @@ __global__ void __launch_bounds__(kItemThreads, 1)
   uint64_t* o_full = p_full + 2;                     // [group][buffer]
   uint64_t* o_free = o_full + 4;                     // [group][buffer]
   uint64_t* drain = o_free + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -608,6 +608,7 @@ __global__ void __launch_bounds__(kItemThreads, 1)
       mbar_init(&o_free[i], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(drain + 1, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -653,38 +654,12 @@ __global__ void __launch_bounds__(kItemThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // MMA warp: warp-uniform control flow, one elected lane issues.
-    // Item k: group g = k & 1, group index i = k >> 1, O buffer b = i & 1.
+    // S issuer: S(k) = Q K^T as soon as item k's Q, K are in and group g's S
+    // buffer is free (PV(k-2) has read the P that S(k) overwrites).  Item k:
+    // group g = k & 1, group index i = k >> 1, O buffer b = i & 1.
     const uint32_t bf = ElemTraits<T>::kBf16;
     const uint32_t idesc_s = idesc_f16(kTile, static_cast<uint32_t>(nc), bf, 0, 0);
-    const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
     const uint64_t base_desc_k = sw128_desc(smem_u32(smem), 16, 1024);
-    const uint64_t base_desc_v = sw128_desc(smem_u32(smem), 8192, 1024);
-    auto issue_pv = [&](int k) -> bool {
-      const int g = k & 1;
-      const int i = k >> 1;
-      const int ob = 2 * g + (i & 1);
-      const int st = k % kItemStages;
-      if (!mbar_wait_warp(&p_full[g], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitMma)) return false;
-      // O buffer ob was last used by item k - 4: its output must have been read.
-      if (i >= 2 && !mbar_wait_warp(&o_free[ob], static_cast<uint32_t>((i >> 1) - 1) & 1u, abort_flag, args.err,
-                                    kErrWaitMma))
-        return false;
-      tc_fence_after();
-      if (elect_one()) {
-        const uint64_t vd = base_desc_v + static_cast<uint64_t>((st * L::kStage + 2 * kQBytes) >> 4);
-        const uint32_t p_col = tmem_base + g * NCOLS;
-#pragma unroll
-        for (int kk = 0; kk < NCOLS / 16; ++kk)
-          if (kk * 16 < nc)
-            umma_f16_ts(tmem_base + kColO + ob * kDimHead, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
-                        kk != 0 ? 1u : 0u);
-        umma_commit(&o_full[ob]);
-        umma_commit(&stage_free[st]);
-      }
-      __syncwarp();
-      return true;
-    };
     bool ok = true;
     for (int k = 0; ok && k < n_local; ++k) {
       const int g = k & 1;
@@ -695,7 +670,6 @@ __global__ void __launch_bounds__(kItemThreads, 1)
         ok = false;
         break;
       }
-      // S(k) overwrites P(k-2) of this group: PV(k-2) must have completed.
       if (i >= 1 && !mbar_wait_warp(&o_full[2 * g + ((i - 1) & 1)], static_cast<uint32_t>((i - 1) >> 1) & 1u,
                                     abort_flag, args.err, kErrWaitMma)) {
         ok = false;
@@ -711,12 +685,45 @@ __global__ void __launch_bounds__(kItemThreads, 1)
         umma_commit(&s_full[g]);
       }
       __syncwarp();
-      if (k > 0 && !issue_pv(k - 1)) ok = false;
     }
-    if (ok && n_local > 0) issue_pv(n_local - 1);
     if (elect_one()) {
       umma_commit(drain);
       wait_drain(drain, 0, args.err);
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // PV issuer: O(k) = P(k) V as soon as item k's P is in TMEM and its O
+    // buffer was read (item k - 4).  PV(k) follows the softmax's read of S(k),
+    // so its commit also covers the Q, K reads of S(k): it frees the stage.
+    const uint32_t bf = ElemTraits<T>::kBf16;
+    const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
+    const uint64_t base_desc_v = sw128_desc(smem_u32(smem), 8192, 1024);
+    for (int k = 0; k < n_local; ++k) {
+      const int g = k & 1;
+      const int i = k >> 1;
+      const int ob = 2 * g + (i & 1);
+      const int st = k % kItemStages;
+      if (!mbar_wait_warp(&p_full[g], static_cast<uint32_t>(i) & 1u, abort_flag, args.err, kErrWaitMma)) break;
+      if (i >= 2 && !mbar_wait_warp(&o_free[ob], static_cast<uint32_t>((i >> 1) - 1) & 1u, abort_flag, args.err,
+                                    kErrWaitMma))
+        break;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint64_t vd = base_desc_v + static_cast<uint64_t>((st * L::kStage + 2 * kQBytes) >> 4);
+        const uint32_t p_col = tmem_base + g * NCOLS;
+#pragma unroll
+        for (int kk = 0; kk < NCOLS / 16; ++kk)
+          if (kk * 16 < nc)
+            umma_f16_ts(tmem_base + kColO + ob * kDimHead, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
+                        kk != 0 ? 1u : 0u);
+        umma_commit(&o_full[ob]);
+        umma_commit(&stage_free[st]);
+      }
+      __syncwarp();
+    }
+    if (elect_one()) {
+      umma_commit(drain + 1);
+      wait_drain(drain + 1, 0, args.err);
     }
     __syncwarp();
   } else {
