@@ -388,9 +388,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int a = 0; a < 8; ++a) mxs[a] = v[a];
 #pragma unroll
-          for (int q = 8; q < 64; q += 16)
+          for (int q = 8; q + 16 <= 64; q += 16)   // columns 8..55
 #pragma unroll
             for (int a = 0; a < 8; ++a) mxs[a] = fmax3(mxs[a], v[q + a], v[q + 8 + a]);
+#pragma unroll
+          for (int a = 0; a < 8; ++a) mxs[a] = fmaxf(mxs[a], v[56 + a]);   // columns 56..63
           const float mx = fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
           // Raise the reference maximum only when this half would exceed 2^8.
           if ((mx - m_ref) * kScaleLog2 > kRescaleLog2) {
@@ -793,44 +795,17 @@ __global__ void __launch_bounds__(kItemThreads, 1)
       tc_fence_after();
       float sum = 1.0f;
       if (active) {
-        // Two passes over S in TMEM, 64 columns at a time (a TMEM load costs
-        // tens of cycles): the row maximum, then exp2, P and the row sum.
-        // Columns >= length (stale, or never written by the N = nc MMA) are
-        // masked.
-        float mxs[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) mxs[a] = -INFINITY;
-#pragma unroll
-        for (int c0 = 0; c0 < NCOLS; c0 += 64) {
-          const int width = NCOLS - c0 < 64 ? NCOLS - c0 : 64;
-          uint32_t ra[32], rb[32];
-          tmem_ld32(s_addr + c0, ra);
-          if (width == 64) tmem_ld32(s_addr + c0 + 32, rb);
-          tmem_wait_ld();
-          reg_fence(ra);
-          if (width == 64) reg_fence(rb);
-#pragma unroll
-          for (int q = 0; q < 64; q += 16) {
-            if (q < width) {
-#pragma unroll
-              for (int a = 0; a < 8; ++a) {
-                const int c1 = c0 + q + a, c2i = c0 + q + 8 + a;
-                const float x1 = c1 < length ? __uint_as_float(q < 32 ? ra[q + a] : rb[q - 32 + a]) : -INFINITY;
-                const float x2 = c2i < length ? __uint_as_float(q < 32 ? ra[q + 8 + a] : rb[q - 24 + a]) : -INFINITY;
-                mxs[a] = fmax3(mxs[a], x1, x2);
-              }
-            }
-          }
-        }
-        const float mx =
-            fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
-        const float mscaled = mx * kScaleLog2;
-        const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
-        const float2 nm2 = make_float2(-mscaled, -mscaled);
+        // One pass over S in TMEM, 64 columns at a time.  Each chunk is
+        // exponentiated against a reference maximum that only has to keep
+        // exp2 below 2^8: it is raised -- and the packed P of earlier chunks
+        // and the running sums rescaled -- only when a chunk exceeds it by
+        // more than 2^8.  Columns >= length (stale, or never written by the
+        // N = nc MMA) are masked.  P (two 16-bit values per column) goes over
+        // the first NCOLS/2 columns of S once all of S is in registers.
+        float m_ref = -INFINITY;
         float2 sums[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                           make_float2(0.f, 0.f)};
-        // P of each 64-column chunk goes over S columns that were already read
-        // (P column c holds keys 2c, 2c+1).
+        uint32_t pk[NCOLS / 2];
 #pragma unroll
         for (int c0 = 0; c0 < NCOLS; c0 += 64) {
           const int width = NCOLS - c0 < 64 ? NCOLS - c0 : 64;
@@ -840,15 +815,47 @@ __global__ void __launch_bounds__(kItemThreads, 1)
           tmem_wait_ld();
           reg_fence(ra);
           if (width == 64) reg_fence(rb);
-          uint32_t pk[32];
+          float v[64];
+#pragma unroll
+          for (int q = 0; q < 64; ++q) {
+            if (q < width) {
+              const float x = __uint_as_float(q < 32 ? ra[q] : rb[q - 32]);
+              v[q] = c0 + q < length ? x : -INFINITY;
+            }
+          }
+          float mxs[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mxs[e] = v[e];
+#pragma unroll
+          for (int q = 8; q < 64; q += 16) {
+            if (q + 16 <= width) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) mxs[e] = fmax3(mxs[e], v[q + e], v[q + 8 + e]);
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mxs[e] = fmaxf(mxs[e], v[width - 8 + e]);   // last 8 columns of the chunk
+          const float mx =
+              fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
+          if ((mx - m_ref) * kScaleLog2 > kRescaleLog2) {
+            const float f = ex2_approx((m_ref - mx) * kScaleLog2);   // 0 when m_ref = -inf
+            m_ref = mx;
+            const float2 f2 = make_float2(f, f);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sums[e] = __fmul2_rn(sums[e], f2);
+            if (c0 > 0) {
+              const uint32_t fp = ElemTraits<T>::pack2(f, f);
+#pragma unroll
+              for (int q = 0; q < c0 / 2; ++q) pk[q] = ElemTraits<T>::mul2(pk[q], fp);
+            }
+          }
+          const float mscaled = m_ref * kScaleLog2;
+          const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
+          const float2 nm2 = make_float2(-mscaled, -mscaled);
 #pragma unroll
           for (int q = 0; q < 64; q += 2) {
             if (q < width) {
-              float v0 = __uint_as_float(q < 32 ? ra[q] : rb[q - 32]);
-              float v1 = __uint_as_float(q < 32 ? ra[q + 1] : rb[q - 31]);
-              if (c0 + q >= length) v0 = -INFINITY;
-              if (c0 + q + 1 >= length) v1 = -INFINITY;
-              const float2 x2 = __ffma2_rn(make_float2(v0, v1), c2, nm2);
+              const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
               float2 p2;
               if (((q >> 1) & 7) < kPolyPairs) {
                 p2 = exp2_poly2(x2);
@@ -857,17 +864,22 @@ __global__ void __launch_bounds__(kItemThreads, 1)
                 p2.y = ex2_approx(x2.y);
               }
               sums[(q >> 1) & 3] = __fadd2_rn(sums[(q >> 1) & 3], p2);
-              pk[q / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
+              pk[(c0 + q) / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
             }
           }
-          if (width == 64) {
-            tmem_st32(s_addr + c0 / 2, pk);
-          } else {
-            uint32_t w[16];
+        }
 #pragma unroll
-            for (int q = 0; q < 16; ++q) w[q] = pk[q];
-            tmem_st16(s_addr + c0 / 2, w);
-          }
+        for (int c = 0; c < NCOLS / 64; ++c) {
+          uint32_t w[32];
+#pragma unroll
+          for (int q = 0; q < 32; ++q) w[q] = pk[32 * c + q];
+          tmem_st32(s_addr + 32 * c, w);
+        }
+        if (NCOLS % 64 == 32) {
+          uint32_t w[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) w[q] = pk[NCOLS / 2 - 16 + q];
+          tmem_st16(s_addr + NCOLS / 2 - 16, w);
         }
         const float2 s01 = __fadd2_rn(__fadd2_rn(sums[0], sums[1]), __fadd2_rn(sums[2], sums[3]));
         sum = s01.x + s01.y;
