@@ -551,13 +551,28 @@ cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, int sm_cou
 // L = 90) does no softmax or output work: the rows of P it leaves stale only
 // reach rows of O that are never stored.
 constexpr int kItemThreads = 352;   // warps: TMA, S issuer, 8 softmax, PV issuer
-constexpr int kItemStages = 4;
+constexpr int kItemStages = 3;
 
 struct ItemSmem {
-  static constexpr int kStage = 3 * kQBytes;   // Q, K, V: 48 KB
-  static constexpr int kBar = kItemStages * kStage;
+  static constexpr int kStage = 3 * kQBytes;           // Q, K, V: 48 KB
+  static constexpr int kOut = kItemStages * kStage;    // per group: the gated output tile, 128 x 64 16-bit
+  static constexpr int kOutBytes = kTile * kDimHead * 2;
+  static constexpr int kBar = kOut + 2 * kOutBytes;
   static constexpr int kBytes = 1024 + kBar + 256;
 };
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_group_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_group_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_group_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Output row of query position `pos` of sequence `seq` (32-bit: rows < 2^31).
 __device__ __forceinline__ int attn_row(const AttnArgs& args, int seq, int pos) {
@@ -569,7 +584,8 @@ __device__ __forceinline__ int attn_row(const AttnArgs& args, int seq, int pos) 
 
 template <typename T, int NCOLS>
 __global__ void __launch_bounds__(kItemThreads, 1)
-    attention_items_kernel(const __grid_constant__ CUtensorMap map, const AttnArgs args) {
+    attention_items_kernel(const __grid_constant__ CUtensorMap map, const __grid_constant__ CUtensorMap map_out,
+                           const AttnArgs args) {
   static_assert(NCOLS % 32 == 0 && NCOLS <= kTile, "score columns per row");
   using L = ItemSmem;
   // TMEM columns: S/P of group g at [g * NCOLS, +NCOLS); O buffer b of group g
@@ -585,8 +601,10 @@ __global__ void __launch_bounds__(kItemThreads, 1)
   uint64_t* p_full = s_full + 2;                     // [group]
   uint64_t* o_full = p_full + 2;                     // [group][buffer]
   uint64_t* o_free = o_full + 4;                     // [group][buffer]
-  uint64_t* drain = o_free + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  uint64_t* drain = o_free + 4;                      // [issuer]
+  uint64_t* out_free = drain + 2;                    // [group]: the output tile may be rewritten
+  uint64_t* out_ready = out_free + 2;                // [group]: all rows of the output tile written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(out_ready + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -611,6 +629,10 @@ __global__ void __launch_bounds__(kItemThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(drain + 1, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&out_free[i], 1);
+      mbar_init(&out_ready[i], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -628,6 +650,7 @@ __global__ void __launch_bounds__(kItemThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch(&map);
+      tma_prefetch(&map_out);
       for (int k = 0; k < n_local; ++k) {
         const int st = k % kItemStages;
         const uint32_t par = static_cast<uint32_t>(k / kItemStages) & 1u;
@@ -735,9 +758,17 @@ __global__ void __launch_bounds__(kItemThreads, 1)
     const bool active = quarter * 32 < length;   // warp-uniform
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem_base + g * NCOLS + lane_off;
-    // Output of the previous item of this group, written after the next softmax.
-    int pend_k = -1, pend_row = 0, pend_head = 0;
+    // Output of the previous item of this group, written after the next
+    // softmax: each warp puts its gated rows into the group's shared-memory
+    // tile (128-byte swizzle) and one thread stores the tile with TMA (rows
+    // past the sequence length fall outside the tensor map and are not
+    // written).  out_free / out_ready hand the tile between the four warps
+    // and that thread (quarter 0, lane 0), with bounded waits.
+    int pend_k = -1;
     float pend_gate = 0.f, pend_sum = 1.f;
+    int outputs = 0;   // tiles this group has stored
+    uint8_t* out_tile = smem + L::kOut + g * L::kOutBytes;
+    const bool issuer = quarter == 0 && lane == 0;
     auto write_output = [&]() -> bool {
       const int i = pend_k >> 1;
       const int ob = 2 * g + (i & 1);
@@ -756,29 +787,46 @@ __global__ void __launch_bounds__(kItemThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[ob]);
+      // The tile is free once the previous store from it has read it.
+      if (outputs > 0) {
+        if (issuer) {
+          bulk_group_wait_read_all();
+          mbar_arrive(&out_free[g]);
+        }
+        if (!mbar_wait_warp(&out_free[g], static_cast<uint32_t>(outputs - 1) & 1u, abort_flag, args.err,
+                            kErrWaitSoftmax))
+          return false;
+      }
       if (active && row < length) {
         const float scale = pend_gate / pend_sum;
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(args.out) + static_cast<long long>(pend_row) * kDimInner +
-                                              pend_head * kDimHead);
+        uint8_t* line = out_tile + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
-        for (int gq = 0; gq < 4; ++gq) {
+        for (int gq = 0; gq < 8; ++gq) {
+          const uint32_t* r = gq < 4 ? &r0[gq * 8] : &r1[(gq - 4) * 8];
           uint4 w;
-          w.x = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 0]) * scale, __uint_as_float(r0[gq * 8 + 1]) * scale);
-          w.y = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 2]) * scale, __uint_as_float(r0[gq * 8 + 3]) * scale);
-          w.z = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 4]) * scale, __uint_as_float(r0[gq * 8 + 5]) * scale);
-          w.w = ElemTraits<T>::pack2(__uint_as_float(r0[gq * 8 + 6]) * scale, __uint_as_float(r0[gq * 8 + 7]) * scale);
-          dst[gq] = w;
-        }
-#pragma unroll
-        for (int gq = 0; gq < 4; ++gq) {
-          uint4 w;
-          w.x = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 0]) * scale, __uint_as_float(r1[gq * 8 + 1]) * scale);
-          w.y = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 2]) * scale, __uint_as_float(r1[gq * 8 + 3]) * scale);
-          w.z = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 4]) * scale, __uint_as_float(r1[gq * 8 + 5]) * scale);
-          w.w = ElemTraits<T>::pack2(__uint_as_float(r1[gq * 8 + 6]) * scale, __uint_as_float(r1[gq * 8 + 7]) * scale);
-          dst[4 + gq] = w;
+          w.x = ElemTraits<T>::pack2(__uint_as_float(r[0]) * scale, __uint_as_float(r[1]) * scale);
+          w.y = ElemTraits<T>::pack2(__uint_as_float(r[2]) * scale, __uint_as_float(r[3]) * scale);
+          w.z = ElemTraits<T>::pack2(__uint_as_float(r[4]) * scale, __uint_as_float(r[5]) * scale);
+          w.w = ElemTraits<T>::pack2(__uint_as_float(r[6]) * scale, __uint_as_float(r[7]) * scale);
+          *reinterpret_cast<uint4*>(line + ((gq ^ (row & 7)) << 4)) = w;
         }
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&out_ready[g]);
+      if (issuer) {
+        if (!mbar_wait(&out_ready[g], static_cast<uint32_t>(outputs) & 1u, abort_flag, args.err, kErrWaitSoftmax))
+          return false;
+        const int item = item_of(pend_k);
+        const int head = item % kHeads;
+        const int seq = item / kHeads;
+        if (args.pos_dim == 1)
+          tma_store_4d(&map_out, out_tile, head * kDimHead, 0, seq % args.d2, seq / args.d2);
+        else
+          tma_store_4d(&map_out, out_tile, head * kDimHead, seq % args.d1, 0, seq / args.d1);
+        bulk_group_commit();
+      }
+      ++outputs;
       return true;
     };
     bool ok = true;
@@ -893,12 +941,11 @@ __global__ void __launch_bounds__(kItemThreads, 1)
         break;
       }
       pend_k = k;
-      pend_row = out_row;
-      pend_head = head;
       pend_gate = gate;
       pend_sum = sum;
     }
     if (ok && pend_k >= 0) write_output();
+    if (issuer) bulk_group_wait_all();   // every tile store has completed before the CTA exits
   }
 
   tc_fence_before();
@@ -920,11 +967,22 @@ cudaError_t launch_items_cols(const CUtensorMap& map, const AttnArgs& args, int 
   }
   const long long items = static_cast<long long>(args.sequences) * kHeads;
   if (items <= 0) return cudaSuccess;
+  // Gated output [rows][512] viewed like the qkv map: (512, d1, d2, d3), one
+  // 64-column head by up to 128 positions per store.
+  const long long rows_all = static_cast<long long>(args.sequences) * args.length;
+  const long long d3 = rows_all / (static_cast<long long>(args.d1) * args.d2);
+  const uint64_t dims[4] = {static_cast<uint64_t>(kDimInner), static_cast<uint64_t>(args.d1),
+                            static_cast<uint64_t>(args.d2), static_cast<uint64_t>(d3)};
+  const uint64_t rb = kDimInner * 2ull;
+  const uint64_t strides[3] = {rb, rb * args.d1, rb * args.d1 * args.d2};
+  const uint32_t box[4] = {64u, args.pos_dim == 1 ? 128u : 1u, args.pos_dim == 2 ? 128u : 1u, 1u};
+  CUtensorMap map_out;
+  if (!make_tmap_4d(&map_out, args.out, 2, dims, strides, box, ElemTraits<T>::kBf16 != 0)) return cudaErrorInvalidValue;
   // The kernel indexes items and output rows in 32 bits.
   const long long rows = static_cast<long long>(args.sequences) * args.length;
   if (items > 0x7FFFFFFFLL || rows > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   const int grid = items < sm_count ? static_cast<int>(items) : sm_count;
-  attention_items_kernel<T, NCOLS><<<grid, kItemThreads, ItemSmem::kBytes, stream>>>(map, args);
+  attention_items_kernel<T, NCOLS><<<grid, kItemThreads, ItemSmem::kBytes, stream>>>(map, map_out, args);
   return cudaGetLastError();
 }
 
