@@ -255,6 +255,8 @@ def main():
                         help="config-4 op-level lines: time/band attention, STFT, band split")
     parser.add_argument("--shard", action="store_true",
                         help="strong scaling: one track's chunks sharded across the ranks, seams by CUDA IPC")
+    parser.add_argument("--stack", action="store_true",
+                        help="config 3: dim-512 / 62-band / hop-441 / GEGLU stack, 16 x 8 s clips, bf16")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -267,6 +269,8 @@ def main():
         return run_shard(args, rank, world, local_rank)
     if args.ops:
         return run_ops(args)
+    if args.stack:
+        return run_stack(args)
 
     import torch
     import torch.distributed as dist
@@ -489,6 +493,108 @@ def run_ops(args):
         line.update({"config": "cfg4 op-level", "data": "synthetic N(0,1)", "dtype": "bf16"})
         print(json.dumps(line), flush=True)
     p.close()
+    return 0
+
+
+def run_stack(args):
+    """Config 3, the layer-level tensor-core benchmark: the configurable stack at
+    dim 512, depth 12, 8 x 64 heads, GEGLU FFN (mult 4), 62 bands, hop 441, bf16
+    operands (random N(0, 0.02) weights, seed 2) on 16 clips of 8 s seeded
+    Gaussian stereo audio (sigma 0.1).  One step = the whole forward of the 16
+    clips (STFT to iSTFT).  value: audio-s/s with the clips resident in HBM;
+    e2e: vocalarc_b200_stack_separate from pinned host buffers."""
+    import torch
+
+    from karaoke_platform_sidecar_native_b200 import native, stack as st
+
+    cfg = st.CONFIG3
+    clips, length = st.CONFIG3_CLIPS, st.CONFIG3_CLIP
+    frames = cfg.frames(length)
+    s = st.Stack(cfg, st.synthetic_weights(cfg, seed=2))
+    rng = np.random.default_rng(2)
+    audio = (rng.standard_normal((clips, 2, length), dtype=np.float32) * np.float32(0.1))
+    d_audio = torch.from_numpy(audio).cuda()
+    d_vocals = torch.empty_like(d_audio)
+    stream = torch.cuda.ExternalStream(s.stream)
+
+    def step():
+        s.forward_device(d_audio, clips, length, d_vocals)
+
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step()
+    s.synchronize()
+    props = torch.cuda.get_device_properties(0)
+    bus = "%08X:%02X:%02X.0" % (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", 0),
+                                getattr(props, "pci_device_id", 0))
+    sampler = ClockSampler([bus])
+    sampler.start()
+    launches0 = s.launch_count
+    s.trace_begin()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    b.record(stream)
+    trace = s.trace_end()
+    s.synchronize()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(b) / args.steps
+    launches = s.launch_count - launches0
+    audio_s = clips * length / 44100.0
+    flops = st.forward_flops(cfg, clips, frames)
+    peaks = load_peaks()
+    kernels = []
+    total = sum(v[1] for v in trace.values())
+    split_bytes = clips * frames * (1025 * 16 + cfg.bands * cfg.dim * 4)   # band split is fp32 SIMT: HBM-bound
+    for name, (count, kms) in sorted(trace.items(), key=lambda kv: -kv[1][1]):
+        entry = {"kernel": name, "launches": count, "total_ms": round(kms, 3), "share": round(kms / total, 4)}
+        if name == "band split" and kms > 0:
+            ach = split_bytes * args.steps / (kms / 1000.0) / 1e9
+            entry.update(achieved_gbs=round(ach, 1), frac=round(ach / peaks["hbm_gbs"], 3))
+        elif name in flops and kms > 0:
+            ach = flops[name] * args.steps / (kms / 1000.0) / 1e12
+            entry.update(achieved_tflops=round(ach, 1), frac=round(ach / peaks["tflops"], 3))
+        kernels.append(entry)
+    all_flop = sum(flops.values())
+    dominant = next(k for k in kernels if "achieved_tflops" in k)
+    # End to end from pinned host memory through the C-ABI.
+    host_in = torch.from_numpy(audio).pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    e_steps = max(1, min(args.steps, 3))
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(e_steps):
+        ok = s.lib.vocalarc_b200_stack_separate(s.handle, native.fptr(host_in.numpy()), clips, length,
+                                                native.fptr(host_out.numpy()))
+        if not ok:
+            raise RuntimeError("vocalarc_b200_stack_separate failed")
+    t1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = t0.elapsed_time(t1) / e_steps
+    if not np.isfinite(host_out.numpy()).all():
+        raise RuntimeError("non-finite vocals")
+    line = {
+        "metric": "audio-seconds separated per second (config 3 stack forward)", "value": round(audio_s / (ms / 1000), 2),
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg3: dim 512, depth 12, 8x64 heads, GEGLU mult 4, 62 bands, n_fft 2048, hop 441, "
+                               "16 clips x 8 s (801 frames) Gaussian sigma 0.1, N(0,0.02) weights seed 2",
+                   "tokens_per_axis": clips * cfg.bands * frames,
+                   "l2": "activations (~7 GB) far larger than the 126 MB L2; no flush"},
+        "forward_tflops": round(all_flop / (ms / 1000) / 1e12, 1),
+        "roofline": {"kernel": dominant["kernel"], "bound": "tensor", "achieved": dominant["achieved_tflops"],
+                     "peak": peaks["tflops"], "unit": "TFLOP/s", "frac": dominant["frac"],
+                     "peak_source": peaks["source"], "traffic": None},
+        "e2e": {"value": round(audio_s / (e_ms / 1000), 2), "unit": UNIT, "h2d_bytes_per_step": int(audio.nbytes),
+                "d2h_bytes_per_step": int(audio.nbytes), "api": "vocalarc_b200_stack_separate (pinned host buffers)"},
+        "gpu_launches": int(launches), "kernels": kernels, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    s.close()
     return 0
 
 

@@ -330,8 +330,64 @@ __device__ __forceinline__ void epilogue_residual(const GemmArgs& args, const CU
   named_barrier(1 + quarter, 64);
   if (half == 0 && valid) {
     const float total = slot[row] + red[(parity * 2 + 1) * 128 + row];
-    args.row_inv_out[R] = 16.0f / sqrtf(total + 1.0e-12f);   // sqrtf(256) / sqrtf(sum + 1e-12)
+    if (args.row_sumsq_out != nullptr)
+      atomicAdd(args.row_sumsq_out + R, total);   // this tile's 256 columns of a wider row
+    else
+      args.row_inv_out[R] = 16.0f / sqrtf(total + 1.0e-12f);   // sqrtf(256) / sqrtf(sum + 1e-12)
   }
+}
+
+// ---------------------------------------------------------------- GEGLU
+// Accumulator columns interleave (value i, gate i) rows of the FFN input
+// projection, so this warp's 128 columns give 64 outputs
+// h = (v inv + b_v) * gelu(g inv + b_g), staged as one 32-row x 64-column block
+// and written by one TMA store at output column (n0 + 128 half) / 2.
+template <typename T>
+__device__ __forceinline__ void epilogue_geglu(const GemmArgs& args, const CUtensorMap* map_out, const TileInfo& ti,
+                                               EpiWarp& ew, uint32_t taddr, int half, int row, long long R, bool valid,
+                                               int row0) {
+  const float inv = (args.row_inv != nullptr && valid) ? __ldg(args.row_inv + R) : 1.0f;
+  const float2 inv2 = make_float2(inv, inv);
+  uint8_t* buf = ew.buf[ew.cur];
+  if (ew.lane == 0) bulk_wait_read1();   // the store that last used this buffer has read it
+  __syncwarp();
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh) {
+    const int c = half * 128 + 32 * hh;
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);
+    tmem_wait_ld();
+    reg_fence(r);
+    const float4* bias = reinterpret_cast<const float4*>(args.bias + ti.n0 + c);
+    float h[16];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = __ldg(bias + q);   // (value, gate, value, gate)
+      const float2 val = __ffma2_rn(make_float2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 2])), inv2,
+                                    make_float2(b.x, b.z));
+      const float2 gate = __ffma2_rn(make_float2(__uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 3])),
+                                     inv2, make_float2(b.y, b.w));
+      const float2 act = __fmul2_rn(val, gelu_pair(gate));
+      h[2 * q] = act.x;
+      h[2 * q + 1] = act.y;
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      uint4 w;
+      w.x = ElemTraits<T>::pack2(h[q * 8 + 0], h[q * 8 + 1]);
+      w.y = ElemTraits<T>::pack2(h[q * 8 + 2], h[q * 8 + 3]);
+      w.z = ElemTraits<T>::pack2(h[q * 8 + 4], h[q * 8 + 5]);
+      w.w = ElemTraits<T>::pack2(h[q * 8 + 6], h[q * 8 + 7]);
+      *reinterpret_cast<uint4*>(buf + sw128(row & 31, 2 * hh + q)) = w;
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (ew.lane == 0) {
+    tma_store_2d(map_out, buf, (ti.n0 + half * 128) >> 1, row0);
+    bulk_commit();
+  }
+  ew.cur ^= 1;
 }
 
 // ---------------------------------------------------------------- direct per-row epilogues
@@ -394,11 +450,11 @@ __device__ __forceinline__ void epilogue_direct(const GemmArgs& args, const Tile
       // is mask component p of the band: frequency first + p/4, channel
       // (p/2)%2, re/im p%2 (mask_band, vocalarc_separation.c:1330-1338).
       const int band = ti.band;
-      const int dim = c_band_dim[band];
-      const int first = c_band_first[band];
+      const int dim = args.band_dim != nullptr ? __ldg(args.band_dim + band) : c_band_dim[band];
+      const int first = args.band_first != nullptr ? __ldg(args.band_first + band) : c_band_first[band];
       const long long seq = R / args.frames;
       const int t = static_cast<int>(R - seq * args.frames);
-      const long long chunk = seq / kBands;
+      const long long chunk = seq / (args.bands > 0 ? args.bands : kBands);
       const float* bias = args.bias + ti.b_row + c;
       const int p0 = n >> 1;
       if (args.mask_ref_layout) {
@@ -596,6 +652,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = ti.a_row + quarter * 32;
       if (EPI == kEpiResidual) {
         epilogue_residual<T>(args, &map_c, &map_d, ti, ew, taddr, half, quarter, row, R, valid, row0, it & 1, red);
+      } else if (EPI == kEpiGeglu) {
+        epilogue_geglu<T>(args, &map_c, ti, ew, taddr, half, row, R, valid, row0);
       } else if ((EPI == kEpiStore || EPI == kEpiGelu || EPI == kEpiQkvRope) && ti.n_size == kBN) {
         epilogue_out16<T, EPI>(args, &map_c, ti, ew, taddr, half, row, R, valid, row0);
       } else {
@@ -641,6 +699,7 @@ cudaError_t dispatch(int epilogue, const GemmMaps& m, const GemmArgs& args, int 
     case kEpiTanhBand: return launch_typed<T, kEpiTanhBand>(m, args, sms, s);
     case kEpiGluMask: return launch_typed<T, kEpiGluMask>(m, args, sms, s);
     case kEpiStoreF32: return launch_typed<T, kEpiStoreF32>(m, args, sms, s);
+    case kEpiGeglu: return launch_typed<T, kEpiGeglu>(m, args, sms, s);
     default: return cudaErrorInvalidValue;
   }
 }

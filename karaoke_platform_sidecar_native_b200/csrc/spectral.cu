@@ -113,7 +113,7 @@ __device__ __forceinline__ void fft32(float2 (&a)[32], const float2* tw) {
 }
 
 __global__ void __launch_bounds__(256, 3) stft_kernel(const float* __restrict__ audio, SegmentMap map, int frames,
-                                                   const float* __restrict__ window,
+                                                   int hop, const float* __restrict__ window,
                                                    const float2* __restrict__ twiddle, float* __restrict__ spec) {
   extern __shared__ float2 stft_smem[];
   float2* tw = stft_smem;
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(256, 3) stft_kernel(const float* __restrict__ 
   const int ch = warp & 1;
   const int c = blockIdx.y;
   const bool active = f < frames;   // warp-uniform; inactive warps only help load the table
-  const int start = f * kHop - kNfft / 2;
+  const int start = f * hop - kNfft / 2;
   // Contiguous source run for frames that need no reflection (warp-uniform).
   long long base = -1;
   if (active && start >= 0 && start + kNfft <= map.seg_length) {
@@ -186,9 +186,13 @@ __global__ void __launch_bounds__(256, 3) stft_kernel(const float* __restrict__ 
 }
 
 // ---------------------------------------------------------------- band split
+// One CTA per (32 frames, band, segment), one thread per output column
+// (DIM = 256 for the bundled model, 512 for a dim-512 stack); the band count
+// is gridDim.y.
 constexpr int kBandFrames = 32;
 
-__global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict__ spec, int frames,
+template <int DIM>
+__global__ void __launch_bounds__(DIM) band_split_kernel(const float* __restrict__ spec, int frames,
                                                          const float* __restrict__ band_wt,
                                                          const long long* __restrict__ band_wt_offset,
                                                          const float* __restrict__ band_gamma,
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int tt = warp; tt < kBandFrames; tt += 8) {
+  for (int tt = warp; tt < kBandFrames; tt += DIM / 32) {
     float* row = rows + tt * d;
     float ss = 0.f;
     for (int k = lane; k < d; k += 32) ss += row[k] * row[k];
@@ -221,16 +225,16 @@ __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict
   }
   __syncthreads();
   const int n = threadIdx.x;
-  const float* wt = band_wt + band_wt_offset[band];  // [d][256]
+  const float* wt = band_wt + band_wt_offset[band];  // [d][DIM]
   float acc[kBandFrames];
-  const float b = band_bias[band * kDim + n];
+  const float b = band_bias[band * DIM + n];
 #pragma unroll
   for (int tt = 0; tt < kBandFrames; ++tt) acc[tt] = b;
   for (int k = 0; k < d; k += 4) {
-    const float w0 = __ldg(wt + (k + 0) * kDim + n);
-    const float w1 = __ldg(wt + (k + 1) * kDim + n);
-    const float w2 = __ldg(wt + (k + 2) * kDim + n);
-    const float w3 = __ldg(wt + (k + 3) * kDim + n);
+    const float w0 = __ldg(wt + (k + 0) * DIM + n);
+    const float w1 = __ldg(wt + (k + 1) * DIM + n);
+    const float w2 = __ldg(wt + (k + 2) * DIM + n);
+    const float w3 = __ldg(wt + (k + 3) * DIM + n);
 #pragma unroll
     for (int tt = 0; tt < kBandFrames; ++tt) {
       const float4 r = *reinterpret_cast<const float4*>(rows + tt * d + k);
@@ -240,10 +244,10 @@ __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict
       acc[tt] = fmaf(r.w, w3, acc[tt]);
     }
   }
-  float* out = x + ((static_cast<long long>(c) * kBands + band) * frames) * kDim + n;
+  float* out = x + ((static_cast<long long>(c) * gridDim.y + band) * frames) * DIM + n;
 #pragma unroll
   for (int tt = 0; tt < kBandFrames; ++tt)
-    if (t0 + tt < frames) out[static_cast<long long>(t0 + tt) * kDim] = acc[tt];
+    if (t0 + tt < frames) out[static_cast<long long>(t0 + tt) * DIM] = acc[tt];
 }
 
 // ---------------------------------------------------------------- row statistics
@@ -275,6 +279,45 @@ __global__ void __launch_bounds__(256) row_stats_kernel(const float* __restrict_
   *reinterpret_cast<uint2*>(dst + lane * 4) = p0;
   *reinterpret_cast<uint2*>(dst + 128 + lane * 4) = p1;
   if (lane == 0) inv[out_row] = 16.0f / sqrtf(ss + 1.0e-12f);   // sqrtf(256) / sqrtf(sum + 1e-12)
+}
+
+// The same statistics for rows of DIM columns (one warp per row, DIM / 128
+// float4 per lane), inv = sqrt(DIM) / sqrt(sum x^2 + 1e-12).
+template <typename T, int DIM>
+__global__ void __launch_bounds__(256) row_stats_dim_kernel(const float* __restrict__ x, long long rows,
+                                                            T* __restrict__ x16, float* __restrict__ inv) {
+  constexpr int kPer = DIM / 128;
+  const long long r = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const float4* src = reinterpret_cast<const float4*>(x + r * DIM);
+  float4 a[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) a[i] = src[32 * i + lane];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) ss += a[i].x * a[i].x + a[i].y * a[i].y + a[i].z * a[i].z + a[i].w * a[i].w;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  T* dst = x16 + r * DIM;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    uint2 p;
+    p.x = ElemTraits<T>::pack2(a[i].x, a[i].y);
+    p.y = ElemTraits<T>::pack2(a[i].z, a[i].w);
+    *reinterpret_cast<uint2*>(dst + 128 * i + lane * 4) = p;
+  }
+  if (lane == 0) inv[r] = sqrtf(static_cast<float>(DIM)) / sqrtf(ss + 1.0e-12f);
+}
+
+// Row factor from the sums of squares that the column tiles of a residual GEMM
+// accumulated, and the sums cleared for the next residual GEMM.
+__global__ void __launch_bounds__(256) norm_finalize_kernel(float* __restrict__ sumsq, float* __restrict__ inv,
+                                                            long long rows, float scale) {
+  const long long r = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  inv[r] = scale / sqrtf(sumsq[r] + 1.0e-12f);
+  sumsq[r] = 0.f;
 }
 
 // ---------------------------------------------------------------- iSTFT
@@ -345,20 +388,21 @@ __global__ void __launch_bounds__(256, 3) istft_frames_kernel(const float* __res
 }
 
 __global__ void __launch_bounds__(256) overlap_add_kernel(const float* __restrict__ frames_buf, int frames,
-                                                          int seg_length, const float* __restrict__ window,
+                                                          int seg_length, int hop, const float* __restrict__ window,
                                                           float* __restrict__ seg_out) {
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= seg_length) return;
   const int cc = blockIdx.y;  // segment * 2 + channel
-  // Frames f with f*512 - 1024 <= s < f*512 + 1024, i.e. f in [q - 3, q] with
-  // q = floor((s + 1024) / 512) (s >= 0, so the division is a floor).
-  const int q = (s + kNfft / 2) / kHop;
+  // Frames f with f*hop - 1024 <= s < f*hop + 1024, i.e. f in
+  // [q - ceil(2048 / hop) + 1, q] with q = floor((s + 1024) / hop) (s >= 0, so
+  // the division is a floor); [q - 3, q] for hop 512.
+  const int q = (s + kNfft / 2) / hop;
   const int f_hi = min(frames - 1, q);
-  const int f_lo = max(0, q - (kNfft / kHop - 1));
+  const int f_lo = max(0, q - ((kNfft + hop - 1) / hop - 1));
   float acc = 0.f, env = 0.f;
   const float* fb = frames_buf + static_cast<long long>(cc) * frames * kNfft;
   for (int f = f_lo; f <= f_hi; ++f) {
-    const int i = s - (f * kHop - kNfft / 2);
+    const int i = s - (f * hop - kNfft / 2);
     if (i < 0 || i >= kNfft) continue;
     acc += fb[static_cast<long long>(f) * kNfft + i];
     const float w = window[i];
@@ -514,8 +558,9 @@ __global__ void __launch_bounds__(256) tta_combine_kernel(const float* __restric
 }  // namespace
 
 cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int frames, const float* window,
-                        const float2* twiddle, float* spec, cudaStream_t stream) {
+                        const float2* twiddle, float* spec, cudaStream_t stream, int hop) {
   if (segments <= 0 || frames <= 0) return cudaSuccess;
+  if (hop <= 0 || hop > kNfft) return cudaErrorInvalidValue;
   static bool configured = false;
   if (!configured) {
     const cudaError_t e = cudaFuncSetAttribute(stft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStftSmem);
@@ -523,23 +568,62 @@ cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int fr
     configured = true;
   }
   stft_kernel<<<dim3((frames + kStftFramesPerCta - 1) / kStftFramesPerCta, segments), 256, kStftSmem, stream>>>(
-      audio, map, frames, window, twiddle, spec);
+      audio, map, frames, hop, window, twiddle, spec);
   return cudaGetLastError();
 }
 
 cudaError_t launch_band_split(const float* spec, int segments, int frames, const float* band_wt,
                               const long long* band_wt_offset, const float* band_gamma, const int* band_gamma_offset,
-                              const float* band_bias, float* x, cudaStream_t stream) {
-  static bool configured = false;
-  const int smem = kBandFrames * 516 * 4;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(band_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    configured = true;
+                              const float* band_bias, float* x, cudaStream_t stream, int dim, int bands) {
+  static bool configured256 = false, configured512 = false;
+  const int smem = kBandFrames * 516 * 4;   // widest band: 129 bins x 2 channels x re/im
+  if (segments <= 0 || frames <= 0 || bands <= 0) return cudaSuccess;
+  dim3 grid((frames + kBandFrames - 1) / kBandFrames, bands, segments);
+  if (dim == 256) {
+    if (!configured256) {
+      cudaError_t e = cudaFuncSetAttribute(band_split_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      configured256 = true;
+    }
+    band_split_kernel<256><<<grid, 256, smem, stream>>>(spec, frames, band_wt, band_wt_offset, band_gamma,
+                                                         band_gamma_offset, band_bias, x);
+  } else if (dim == 512) {
+    if (!configured512) {
+      cudaError_t e = cudaFuncSetAttribute(band_split_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      configured512 = true;
+    }
+    band_split_kernel<512><<<grid, 512, smem, stream>>>(spec, frames, band_wt, band_wt_offset, band_gamma,
+                                                         band_gamma_offset, band_bias, x);
+  } else {
+    return cudaErrorInvalidValue;
   }
-  dim3 grid((frames + kBandFrames - 1) / kBandFrames, kBands, segments);
-  band_split_kernel<<<grid, 256, smem, stream>>>(spec, frames, band_wt, band_wt_offset, band_gamma,
-                                                  band_gamma_offset, band_bias, x);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_row_stats_dim(const float* x, long long rows, int dim, void* x16, float* inv, bool bf16,
+                                 cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  if (dim == 256) {
+    if (bf16)
+      row_stats_dim_kernel<__nv_bfloat16, 256><<<blocks, 256, 0, stream>>>(x, rows, static_cast<__nv_bfloat16*>(x16), inv);
+    else
+      row_stats_dim_kernel<__half, 256><<<blocks, 256, 0, stream>>>(x, rows, static_cast<__half*>(x16), inv);
+  } else if (dim == 512) {
+    if (bf16)
+      row_stats_dim_kernel<__nv_bfloat16, 512><<<blocks, 256, 0, stream>>>(x, rows, static_cast<__nv_bfloat16*>(x16), inv);
+    else
+      row_stats_dim_kernel<__half, 512><<<blocks, 256, 0, stream>>>(x, rows, static_cast<__half*>(x16), inv);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_norm_finalize(float* sumsq, float* inv, long long rows, float scale, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  norm_finalize_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, stream>>>(sumsq, inv, rows, scale);
   return cudaGetLastError();
 }
 
@@ -572,10 +656,11 @@ cudaError_t launch_istft_frames(const float* spec, const float* mask, int segmen
 }
 
 cudaError_t launch_overlap_add(const float* frames_buf, int segments, int frames, int seg_length, const float* window,
-                               float* seg_out, cudaStream_t stream) {
+                               float* seg_out, cudaStream_t stream, int hop) {
   if (segments <= 0 || seg_length <= 0) return cudaSuccess;
+  if (hop <= 0 || hop > kNfft) return cudaErrorInvalidValue;
   dim3 grid((seg_length + 255) / 256, segments * 2);
-  overlap_add_kernel<<<grid, 256, 0, stream>>>(frames_buf, frames, seg_length, window, seg_out);
+  overlap_add_kernel<<<grid, 256, 0, stream>>>(frames_buf, frames, seg_length, hop, window, seg_out);
   return cudaGetLastError();
 }
 

@@ -33,6 +33,8 @@ enum EpilogueKind : int {
   kEpiTanhBand = 4,   // grouped mask layer 1: out_16[r][n0+c] = tanh(acc * inv[r] + bias[b_row + c])
   kEpiGluMask = 5,    // grouped mask layer 2: GLU pairs scattered into the complex mask
   kEpiStoreF32 = 6,   // out_f32[r][n] = acc (tests)
+  kEpiGeglu = 7,      // columns interleave (value i, gate i): out_16[r][n/2] = value * gelu(gate), both
+                      // acc * inv[r] + bias (staged TMA store)
 };
 
 // Tensor maps of one GEMM launch: A and B operands; c = the staged output
@@ -66,6 +68,16 @@ struct GemmArgs {
   int frames;           // mask: frames per chunk (T)
   int mask_ref_layout;  // mask: 1 = reference [1025][2][T][2], 0 = frame-major [C][T][1025][2][2]
   int* err;
+  // kEpiResidual over N > 256: each column tile adds its share of sum x^2 to
+  // row_sumsq_out[r] (zeroed beforehand; two tiles per row add in either order
+  // to the same float) instead of writing row_inv_out.
+  float* row_sumsq_out;
+  // kEpiGluMask for a model other than the bundled one: band count and the
+  // per-band first bin / 4 * width tables in global memory (0 / null = the
+  // bundled 90-band tables).
+  int bands;
+  const int* band_first;
+  const int* band_dim;
 };
 
 // Grouped-tile metadata packing: m_valid (8 bits) | n_size (9 bits) << 8 | band << 17.
@@ -121,11 +133,20 @@ inline SegmentMap demix_map(int length, int chunk, int border, int padded, int s
 }
 
 cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int frames,
-                        const float* window, const float2* twiddle, float* spec, cudaStream_t stream);
+                        const float* window, const float2* twiddle, float* spec, cudaStream_t stream,
+                        int hop = kHop);
+// Band split into `dim` (256 or 512) columns over `bands` bands; x rows are
+// (segment * bands + band) * frames + frame.
 cudaError_t launch_band_split(const float* spec, int segments, int frames, const float* band_wt,
                               const long long* band_wt_offset, const float* band_gamma,
                               const int* band_gamma_offset, const float* band_bias, float* x,
-                              cudaStream_t stream);
+                              cudaStream_t stream, int dim = kDim, int bands = kBands);
+// Row statistics of a [rows][dim] fp32 residual (dim 256 or 512): x16 and
+// inv = sqrt(dim) / sqrt(sum x^2 + 1e-12).
+cudaError_t launch_row_stats_dim(const float* x, long long rows, int dim, void* x16, float* inv, bool bf16,
+                                 cudaStream_t stream);
+// inv[r] = scale / sqrt(sumsq[r] + 1e-12), then sumsq[r] = 0.
+cudaError_t launch_norm_finalize(float* sumsq, float* inv, long long rows, float scale, cudaStream_t stream);
 // Row statistics of the fp32 residual: x16 = 16-bit copy of x and
 // inv = sqrt(256) / sqrt(sum x^2 + 1e-12) per row.  With remap_s0 > 0 the rows
 // of a physical [remap_s0][remap_l0] token grid are written as [l0][s0].
@@ -135,7 +156,7 @@ cudaError_t launch_istft_frames(const float* spec, const float* mask, int segmen
                                 const float* window, const float2* twiddle, float* frames_out,
                                 cudaStream_t stream);
 cudaError_t launch_overlap_add(const float* frames_buf, int segments, int frames, int seg_length,
-                               const float* window, float* seg_out, cudaStream_t stream);
+                               const float* window, float* seg_out, cudaStream_t stream, int hop = kHop);
 cudaError_t launch_demix(const float* seg_out, SegmentMap map, int chunks, int model_batch,
                          float* vocals, cudaStream_t stream);
 // One contiguous chunk range of a track sharded across GPUs: padded samples

@@ -18,7 +18,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB_PATH = os.path.join(HERE, "libvocalarc_b200.so")
-HEADERS = (os.path.join(ROOT, "include", "native_gpu.h"), os.path.join(ROOT, "include", "vocalarc_b200.h"))
+HEADERS = (os.path.join(ROOT, "include", "native_gpu.h"), os.path.join(ROOT, "include", "vocalarc_b200.h"),
+           os.path.join(ROOT, "include", "vocalarc_b200_stack.h"))
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _vp = ctypes.c_void_p

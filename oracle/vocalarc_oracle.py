@@ -71,17 +71,21 @@ def reflect_index(index: np.ndarray, length: int) -> np.ndarray:
     return np.where(r >= length, period - r, r)
 
 
-def frames_for(length: int) -> int:
-    return length // HOP + 1
+def frames_for(length: int, hop: int = HOP) -> int:
+    return length // hop + 1
 
 
-def stft(audio: np.ndarray) -> np.ndarray:
-    """Planar ``[2][len]`` audio -> ``source[1025][2][T][2]`` (reference layout)."""
+def stft(audio: np.ndarray, hop: int = HOP) -> np.ndarray:
+    """Planar ``[2][len]`` audio -> ``source[1025][2][T][2]`` (reference layout).
+
+    ``hop`` other than 512 is the same framing with another frame step (the
+    configurable stack's STFT; the reference only has 512).
+    """
     audio = np.asarray(audio, dtype=F32)
     length = audio.shape[1]
-    frames = frames_for(length)
+    frames = frames_for(length, hop)
     win = window()
-    starts = np.arange(frames, dtype=np.int64) * HOP - NFFT // 2
+    starts = np.arange(frames, dtype=np.int64) * hop - NFFT // 2
     idx = reflect_index(starts[:, None] + np.arange(NFFT)[None, :], length)
     out = np.empty((FREQ_BINS, CHANNELS, frames, 2), dtype=F32)
     for ch in range(CHANNELS):
@@ -239,7 +243,7 @@ def mask_estimate(model, features: np.ndarray) -> np.ndarray:
     return mask
 
 
-def istft(source: np.ndarray, mask: np.ndarray, length: int) -> np.ndarray:
+def istft(source: np.ndarray, mask: np.ndarray, length: int, hop: int = HOP) -> np.ndarray:
     """Masked inverse STFT with the native normalisation rule -> ``[2][length]``."""
     frames = source.shape[2]
     win = window()
@@ -257,7 +261,7 @@ def istft(source: np.ndarray, mask: np.ndarray, length: int) -> np.ndarray:
         time = np.fft.ifft(full, axis=0).real                        # includes / 2048
         contrib = (time * win.astype(np.float64)[:, None]).astype(F32)  # [2048][T]
         for frame in range(frames):
-            start = frame * HOP - NFFT // 2
+            start = frame * hop - NFFT // 2
             lo, hi = max(0, start), min(length, start + NFFT)
             if lo >= hi:
                 continue
