@@ -257,6 +257,8 @@ def main():
                         help="strong scaling: one track's chunks sharded across the ranks, seams by CUDA IPC")
     parser.add_argument("--stack", action="store_true",
                         help="config 3: dim-512 / 62-band / hop-441 / GEGLU stack, 16 x 8 s clips, bf16")
+    parser.add_argument("--clips", type=int, default=0, help="--stack: clips per forward (default 16)")
+    parser.add_argument("--depth", type=int, default=0, help="--stack: layers (default 12; fewer for profiling)")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -507,8 +509,8 @@ def run_stack(args):
 
     from karaoke_platform_sidecar_native_b200 import native, stack as st
 
-    cfg = st.CONFIG3
-    clips, length = st.CONFIG3_CLIPS, st.CONFIG3_CLIP
+    cfg = st.CONFIG3.replace(depth=args.depth) if args.depth > 0 else st.CONFIG3
+    clips, length = (args.clips if args.clips > 0 else st.CONFIG3_CLIPS), st.CONFIG3_CLIP
     frames = cfg.frames(length)
     s = st.Stack(cfg, st.synthetic_weights(cfg, seed=2))
     rng = np.random.default_rng(2)
@@ -581,8 +583,8 @@ def run_stack(args):
         "metric": "audio-seconds separated per second (config 3 stack forward)", "value": round(audio_s / (ms / 1000), 2),
         "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "cfg3: dim 512, depth 12, 8x64 heads, GEGLU mult 4, 62 bands, n_fft 2048, hop 441, "
-                               "16 clips x 8 s (801 frames) Gaussian sigma 0.1, N(0,0.02) weights seed 2",
+        "config": {"workload": f"cfg3: dim 512, depth {cfg.depth}, 8x64 heads, GEGLU mult 4, 62 bands, n_fft 2048, "
+                               f"hop 441, {clips} clips x 8 s (801 frames) Gaussian sigma 0.1, N(0,0.02) weights seed 2",
                    "tokens_per_axis": clips * cfg.bands * frames,
                    "l2": "activations (~7 GB) far larger than the 126 MB L2; no flush"},
         "forward_tflops": round(all_flop / (ms / 1000) / 1e12, 1),
