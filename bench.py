@@ -287,7 +287,11 @@ def main():
     provider = native.Provider(local_rank)
     if args.precision == "bf16":
         provider.set_precision(True)
-    provider.load_model(modelpack.synthetic_pack(**modelpack.BENCH_RECIPE))
+    pack = modelpack.synthetic_pack(**modelpack.BENCH_RECIPE)
+    t_load = time.perf_counter()
+    provider.load_model(pack)
+    model_load = {"ms": round((time.perf_counter() - t_load) * 1000.0, 1), "from_cache": provider.model_from_cache,
+                  "pack_bytes": len(pack)}
     length = int(args.seconds * 44100)
     audio = fixtures.long_mix(args.seconds, seed=1 + rank)
     d_audio = torch.from_numpy(audio).cuda()
@@ -413,6 +417,7 @@ def main():
                     "d2h_bytes_per_step": int(audio.nbytes), "steps": e2e_steps,
                     "api": "vocalarc_b200_separate_chunked (C-ABI, pinned host buffers)"},
             "gpu_launches": int(launches),
+            "model_load": model_load,
             "roofline": roofline,
             "kernels": kernels,
             "cpu_baseline": cpu,

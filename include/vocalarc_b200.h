@@ -32,6 +32,24 @@ native_gpu *vocalarc_b200_create(int device);
    is not retained. */
 int vocalarc_b200_load_model(native_gpu *gpu, const void *pack, size_t bytes);
 
+/* The same from a pack file, read through mmap (no copy of the file in memory). */
+int vocalarc_b200_load_model_file(native_gpu *gpu, const char *path);
+
+/* Load fast path.  load_model lays out every device pointer first, then takes
+   the converted weights (16-bit K-major, gammas folded, mask rows interleaved:
+   the exact bytes of the device allocation) from an image file keyed by the
+   pack's content hash and the precision, or converts them on several threads
+   (VOCALARC_B200_LOAD_THREADS) and writes that file.  Images live in
+   VOCALARC_B200_IMAGE_CACHE ("off" disables), else $XDG_CACHE_HOME/vocalarc-b200,
+   else $HOME/.cache/vocalarc-b200.  model_from_cache: 1 when the last load used
+   an image.  model_image builds the image on the host alone (no GPU; out NULL
+   queries the size); store_model_image writes it to the cache directory ahead
+   of the first load and returns its path. */
+int vocalarc_b200_model_from_cache(const native_gpu *gpu);
+int vocalarc_b200_model_image(const void *pack, size_t bytes, int bf16, int threads, void *out, size_t capacity,
+                              size_t *image_bytes);
+int vocalarc_b200_store_model_image(const void *pack, size_t bytes, int bf16, char *path_out, int capacity);
+
 /* Whole-clip forward: frames = length/512 + 1, exactly forward_model. */
 int vocalarc_b200_separate(native_gpu *gpu, const float *audio, int length, float *vocals);
 

@@ -12,12 +12,20 @@
 // band-major rows directly as its per-band A operand.  Every RMSNorm gamma is
 // folded into the weights of the GEMM that consumes the norm, and the GEMM
 // that updates x writes the per-row factor sqrt(256)/|x| next to x16.
+#include <atomic>
+#include <cerrno>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
+
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -137,15 +145,23 @@ struct BandW {
   float* bias = nullptr;        // [90][256]
 };
 
-// Bump allocator over one cudaMalloc.
+// Bump allocator over one cudaMalloc.  With `host` set, weights are written
+// to a host mirror of [base, base + cap) and reach the device in one copy
+// later; with `dry` set, only pointers (and tensor maps) are laid out.
 struct Arena {
   char* base = nullptr;
   size_t cap = 0, used = 0;
+  uint8_t* host = nullptr;
+  bool dry = false;
+  bool maps = true;
+  uint64_t layout = 1469598103934665603ull;   // hash of every (offset, size) taken
   void* take(size_t bytes) {
     const size_t off = (used + 1023) & ~size_t(1023);
     if (off + bytes > cap) return nullptr;
     used = off + bytes;
-    return base + off;
+    layout = (layout ^ off) * 1099511628211ull;
+    layout = (layout ^ bytes) * 1099511628211ull;
+    return reinterpret_cast<void*>(reinterpret_cast<uintptr_t>(base) + off);
   }
 };
 
@@ -191,6 +207,7 @@ struct native_gpu {
   int n_tiles2 = 0;
   // loaded model (vocalarc_b200_load_model)
   int model_loaded = 0;
+  int model_from_cache = 0;     // the loaded weights came from a converted image on disk
   void* model_mem = nullptr;
   BlockW blocks[kDepth][2];
   BandW band;
@@ -372,23 +389,36 @@ void scale_columns(std::vector<float>& w, int in, const float* scale) {
     for (int i = 0; i < in; ++i) w[r * in + i] *= scale[i];
 }
 
+// Weight bytes for `dst` (a pointer of `arena`): into the host mirror, or
+// straight to the device; nothing in a layout-only pass.
+bool put(native_gpu* g, Arena& arena, void* dst, const void* src, size_t bytes, const char* what) {
+  if (arena.dry) return true;
+  if (arena.host != nullptr) {
+    memcpy(arena.host + (reinterpret_cast<uintptr_t>(dst) - reinterpret_cast<uintptr_t>(arena.base)), src, bytes);
+    return true;
+  }
+  return cuda_ok(g, cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice), what);
+}
+
 bool upload16(native_gpu* g, Arena& arena, const float* packed, int in, int out, void** dst, CUtensorMap* map,
               int box_rows, const float* col_scale = nullptr) {
-  std::vector<float> w;
-  std::vector<uint16_t> h;
-  unpack_packed(packed, in, out, w);
-  if (col_scale != nullptr) scale_columns(w, in, col_scale);
-  to16(w, g->bf16 != 0, h);
-  *dst = arena.take(h.size() * 2);
+  *dst = arena.take(static_cast<size_t>(in) * out * 2);
   if (*dst == nullptr) return false;
-  if (!cuda_ok(g, cudaMemcpy(*dst, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "upload weight")) return false;
-  return make_map_rows(g, map, *dst, out, in, box_rows);
+  if (!arena.dry) {
+    std::vector<float> w;
+    std::vector<uint16_t> h;
+    unpack_packed(packed, in, out, w);
+    if (col_scale != nullptr) scale_columns(w, in, col_scale);
+    to16(w, g->bf16 != 0, h);
+    if (!put(g, arena, *dst, h.data(), h.size() * 2, "upload weight")) return false;
+  }
+  return !arena.maps || make_map_rows(g, map, *dst, out, in, box_rows);
 }
 
 bool upload_f32(native_gpu* g, Arena& arena, const float* src, size_t count, float** dst) {
   *dst = static_cast<float*>(arena.take(count * 4));
   if (*dst == nullptr) return false;
-  return cuda_ok(g, cudaMemcpy(*dst, src, count * 4, cudaMemcpyHostToDevice), "upload vector");
+  return put(g, arena, *dst, src, count * 4, "upload vector");
 }
 
 constexpr size_t kBlockBytes = (static_cast<size_t>(kQkvRows) * kDim + kDim * kDimInner + 2 * kFfDim * kDim) * 2 +
@@ -396,18 +426,20 @@ constexpr size_t kBlockBytes = (static_cast<size_t>(kQkvRows) * kDim + kDim * kD
 
 bool upload_block(native_gpu* g, Arena& arena, const native_gpu_transformer_weights& w, BlockW& b) {
   // q|k|v rows, then the gate rows, then zero rows; all scaled by the attention gamma.
-  std::vector<float> qkv, gw;
-  unpack_packed(w.qkv, kDim, kQkvDim, qkv);
-  unpack_packed(w.gate_weight, kDim, kHeads, gw);
-  qkv.resize(static_cast<size_t>(kQkvRows) * kDim, 0.f);
-  std::copy(gw.begin(), gw.end(), qkv.begin() + static_cast<size_t>(kQkvDim) * kDim);
-  scale_columns(qkv, kDim, w.gamma);
-  std::vector<uint16_t> h;
-  to16(qkv, g->bf16 != 0, h);
-  b.qkv = arena.take(h.size() * 2);
-  if (b.qkv == nullptr || !cuda_ok(g, cudaMemcpy(b.qkv, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "qkv"))
-    return false;
-  if (!make_map_rows(g, &b.m_qkv, b.qkv, kQkvRows, kDim, 256)) return false;
+  b.qkv = arena.take(static_cast<size_t>(kQkvRows) * kDim * 2);
+  if (b.qkv == nullptr) return false;
+  if (!arena.dry) {
+    std::vector<float> qkv, gw;
+    unpack_packed(w.qkv, kDim, kQkvDim, qkv);
+    unpack_packed(w.gate_weight, kDim, kHeads, gw);
+    qkv.resize(static_cast<size_t>(kQkvRows) * kDim, 0.f);
+    std::copy(gw.begin(), gw.end(), qkv.begin() + static_cast<size_t>(kQkvDim) * kDim);
+    scale_columns(qkv, kDim, w.gamma);
+    std::vector<uint16_t> h;
+    to16(qkv, g->bf16 != 0, h);
+    if (!put(g, arena, b.qkv, h.data(), h.size() * 2, "qkv")) return false;
+  }
+  if (arena.maps && !make_map_rows(g, &b.m_qkv, b.qkv, kQkvRows, kDim, 256)) return false;
   if (!upload16(g, arena, w.out_weight, kDimInner, kDim, &b.out, &b.m_out, 256) ||
       !upload16(g, arena, w.ff1_weight, kDim, kFfDim, &b.ff1, &b.m_ff1, 256, w.ff_gamma) ||
       !upload16(g, arena, w.ff2_weight, kFfDim, kDim, &b.ff2, &b.m_ff2, 256))
@@ -430,44 +462,66 @@ constexpr size_t mask_bytes_estimate() {
 // Mask head weights: first layers stacked [90*1024][256]; second layers with
 // rows interleaved (value i, gate i) so the GLU pairs are adjacent columns,
 // each band padded to a multiple of 16 rows.
-bool upload_mask(native_gpu* g, Arena& arena, const native_gpu_mask_band* bands, const float* final_gamma, MaskW& m) {
+// Bands [band_lo, band_hi) are converted (the layout is always the whole head,
+// so several calls over one arena can split the work); write_bias also
+// converts the bias vectors.
+bool upload_mask(native_gpu* g, Arena& arena, const native_gpu_mask_band* bands, const float* final_gamma, MaskW& m,
+                 int band_lo = 0, int band_hi = kBands, bool write_bias = true) {
   const bool bf = g->bf16 != 0;
-  std::vector<float> w, all1(static_cast<size_t>(kBands) * kFfDim * kDim), b1(static_cast<size_t>(kBands) * kFfDim);
-  for (int b = 0; b < kBands; ++b) {
-    unpack_packed(bands[b].first_weight, kDim, kFfDim, w);
-    scale_columns(w, kDim, final_gamma);   // the final RMSNorm gamma, folded
-    memcpy(&all1[static_cast<size_t>(b) * kFfDim * kDim], w.data(), w.size() * 4);
-    memcpy(&b1[static_cast<size_t>(b) * kFfDim], bands[b].first_bias, kFfDim * 4);
-  }
-  std::vector<uint16_t> h;
-  to16(all1, bf, h);
-  m.w1 = arena.take(h.size() * 2);
-  if (m.w1 == nullptr || !cuda_ok(g, cudaMemcpy(m.w1, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "mask w1"))
-    return false;
-  if (!make_map_rows(g, &m.m_w1, m.w1, static_cast<long long>(kBands) * kFfDim, kDim, 256)) return false;
-  if (!upload_f32(g, arena, b1.data(), b1.size(), &m.b1)) return false;
-  m.w2_total = mask_w2_rows_total();
-  std::vector<float> all2(static_cast<size_t>(m.w2_total) * kFfDim, 0.f), b2(m.w2_total, 0.f);
   int off = 0;
   for (int b = 0; b < kBands; ++b) {
-    const int d = bands[b].input_dim;
-    unpack_packed(bands[b].second_weight, kFfDim, 2 * d, w);
-    for (int i = 0; i < d; ++i) {
-      memcpy(&all2[static_cast<size_t>(off + 2 * i) * kFfDim], &w[static_cast<size_t>(i) * kFfDim], kFfDim * 4);
-      memcpy(&all2[static_cast<size_t>(off + 2 * i + 1) * kFfDim], &w[static_cast<size_t>(d + i) * kFfDim], kFfDim * 4);
-      b2[off + 2 * i] = bands[b].second_bias[i];
-      b2[off + 2 * i + 1] = bands[b].second_bias[d + i];
-    }
     m.w2_off[b] = off;
-    m.w2_rows[b] = round16(2 * d);
+    m.w2_rows[b] = round16(2 * bands[b].input_dim);
     off += m.w2_rows[b];
   }
-  to16(all2, bf, h);
-  m.w2 = arena.take(h.size() * 2);
-  if (m.w2 == nullptr || !cuda_ok(g, cudaMemcpy(m.w2, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "mask w2"))
-    return false;
-  if (!make_map_rows(g, &m.m_w2, m.w2, m.w2_total, kFfDim, 16)) return false;
-  return upload_f32(g, arena, b2.data(), b2.size(), &m.b2);
+  m.w2_total = off;
+  std::vector<float> w, rows, bias;
+  std::vector<uint16_t> h;
+  // Layer 1, band by band: [1024][256] with the final RMSNorm gamma folded.
+  const size_t w1_band = static_cast<size_t>(kFfDim) * kDim;
+  m.w1 = arena.take(kBands * w1_band * 2);
+  if (m.w1 == nullptr) return false;
+  if (!arena.dry) {
+    bias.resize(static_cast<size_t>(kBands) * kFfDim);
+    for (int b = 0; b < kBands; ++b) memcpy(&bias[static_cast<size_t>(b) * kFfDim], bands[b].first_bias, kFfDim * 4);
+    for (int b = band_lo; b < band_hi; ++b) {
+      unpack_packed(bands[b].first_weight, kDim, kFfDim, w);
+      scale_columns(w, kDim, final_gamma);
+      to16(w, bf, h);
+      if (!put(g, arena, static_cast<char*>(m.w1) + b * w1_band * 2, h.data(), w1_band * 2, "mask w1")) return false;
+    }
+  }
+  if (arena.maps && !make_map_rows(g, &m.m_w1, m.w1, static_cast<long long>(kBands) * kFfDim, kDim, 256)) return false;
+  m.b1 = static_cast<float*>(arena.take(static_cast<size_t>(kBands) * kFfDim * 4));
+  if (m.b1 == nullptr || (write_bias && !put(g, arena, m.b1, bias.data(), bias.size() * 4, "mask b1"))) return false;
+  // Layer 2, band by band: rows interleaved (value i, gate i), zero rows up to a multiple of 16.
+  m.w2 = arena.take(static_cast<size_t>(m.w2_total) * kFfDim * 2);
+  if (m.w2 == nullptr) return false;
+  if (!arena.dry) {
+    bias.assign(m.w2_total, 0.f);
+    for (int b = 0; b < kBands; ++b)
+      for (int i = 0; i < bands[b].input_dim; ++i) {
+        bias[m.w2_off[b] + 2 * i] = bands[b].second_bias[i];
+        bias[m.w2_off[b] + 2 * i + 1] = bands[b].second_bias[bands[b].input_dim + i];
+      }
+    for (int b = band_lo; b < band_hi; ++b) {
+      const int d = bands[b].input_dim;
+      const int o = m.w2_off[b];
+      unpack_packed(bands[b].second_weight, kFfDim, 2 * d, w);
+      rows.assign(static_cast<size_t>(m.w2_rows[b]) * kFfDim, 0.f);
+      for (int i = 0; i < d; ++i) {
+        memcpy(&rows[static_cast<size_t>(2 * i) * kFfDim], &w[static_cast<size_t>(i) * kFfDim], kFfDim * 4);
+        memcpy(&rows[static_cast<size_t>(2 * i + 1) * kFfDim], &w[static_cast<size_t>(d + i) * kFfDim], kFfDim * 4);
+      }
+      to16(rows, bf, h);
+      if (!put(g, arena, static_cast<char*>(m.w2) + static_cast<size_t>(o) * kFfDim * 2, h.data(), h.size() * 2,
+               "mask w2"))
+        return false;
+    }
+  }
+  if (arena.maps && !make_map_rows(g, &m.m_w2, m.w2, m.w2_total, kFfDim, 16)) return false;
+  m.b2 = static_cast<float*>(arena.take(static_cast<size_t>(m.w2_total) * 4));
+  return m.b2 != nullptr && (!write_bias || put(g, arena, m.b2, bias.data(), bias.size() * 4, "mask b2"));
 }
 
 bool ensure_mask_tiles(native_gpu* g, int frames, const MaskW& m) {
@@ -749,6 +803,326 @@ struct PackCursor {
   }
 };
 
+// Tensor pointers of one VSCNAT01 pack (model_parse, vocalarc_separation.c:528-589).
+struct PackView {
+  native_gpu_transformer_weights layers[kDepth][2];
+  const float* bg[kBands];
+  const float* bw[kBands];
+  const float* bb[kBands];
+  const float* final_gamma = nullptr;
+  native_gpu_mask_band mb[kBands];
+};
+
+bool parse_pack_view(const void* pack, size_t bytes, PackView& v) {
+  if (pack == nullptr || bytes < 64) return false;
+  const unsigned char* base = static_cast<const unsigned char*>(pack);
+  uint32_t fields[14];
+  memcpy(fields, base + 8, sizeof(fields));
+  const uint32_t expect[12] = {1, kDim, kDepth, kBands, kHeads, kDimHead, kFreqBins, kChannels, kNfft, kHop, kNfft,
+                               kModelFrames};
+  if (memcmp(base, "VSCNAT01", 8) != 0 || memcmp(fields, expect, sizeof(expect)) != 0) {
+    fprintf(stderr, "vocalarc-b200: unsupported native model header\n");
+    return false;
+  }
+  PackCursor cur{base + 64, base + bytes};
+  for (int l = 0; l < kDepth; ++l)
+    for (int a = 0; a < 2; ++a) {
+      native_gpu_transformer_weights& w = v.layers[l][a];
+      w.gamma = cur.next(kDim);
+      w.qkv = cur.next(static_cast<uint64_t>(kQkvDim) * kDim);
+      w.gate_weight = cur.next(kHeads * kDim);
+      w.gate_bias = cur.next(kHeads);
+      w.out_weight = cur.next(static_cast<uint64_t>(kDim) * kDimInner);
+      w.ff_gamma = cur.next(kDim);
+      w.ff1_weight = cur.next(static_cast<uint64_t>(kFfDim) * kDim);
+      w.ff1_bias = cur.next(kFfDim);
+      w.ff2_weight = cur.next(static_cast<uint64_t>(kDim) * kFfDim);
+      w.ff2_bias = cur.next(kDim);
+      if (!w.gamma || !w.qkv || !w.gate_weight || !w.gate_bias || !w.out_weight || !w.ff_gamma || !w.ff1_weight ||
+          !w.ff1_bias || !w.ff2_weight || !w.ff2_bias) {
+        fprintf(stderr, "vocalarc-b200: native model truncated in layer %d\n", l);
+        return false;
+      }
+    }
+  for (int b = 0; b < kBands; ++b) {
+    const int d = 4 * kBandFreqs[b];
+    v.bg[b] = cur.next(d);
+    v.bw[b] = cur.next(static_cast<uint64_t>(kDim) * d);
+    v.bb[b] = cur.next(kDim);
+    if (!v.bg[b] || !v.bw[b] || !v.bb[b]) return false;
+  }
+  v.final_gamma = cur.next(kDim);
+  if (v.final_gamma == nullptr) return false;
+  for (int b = 0; b < kBands; ++b) {
+    const int d = 4 * kBandFreqs[b];
+    v.mb[b].first_weight = cur.next(static_cast<uint64_t>(kFfDim) * kDim);
+    v.mb[b].first_bias = cur.next(kFfDim);
+    v.mb[b].second_weight = cur.next(static_cast<uint64_t>(2 * d) * kFfDim);
+    v.mb[b].second_bias = cur.next(2 * d);
+    v.mb[b].input_dim = d;
+    v.mb[b].first_frequency = band_first(b);
+    if (!v.mb[b].first_weight || !v.mb[b].first_bias || !v.mb[b].second_weight || !v.mb[b].second_bias) return false;
+  }
+  return true;
+}
+
+// Band split for the SIMT kernel: W^T per band ([d_b][256]), gammas in bin
+// order, biases [90][256], and the two offset tables.
+bool upload_band(native_gpu* g, Arena& arena, const PackView& v, BandW& out) {
+  std::vector<long long> wt_off(kBands);
+  std::vector<int> g_off(kBands + 1);
+  size_t cur_wt = 0;
+  int cur_g = 0;
+  for (int b = 0; b < kBands; ++b) {
+    const int d = 4 * kBandFreqs[b];
+    wt_off[b] = static_cast<long long>(cur_wt);
+    cur_wt += static_cast<size_t>(d) * kDim;
+    g_off[b] = cur_g;
+    cur_g += d;
+  }
+  g_off[kBands] = cur_g;
+  std::vector<float> wt, gam, bias, w;
+  if (!arena.dry) {
+    wt.resize(static_cast<size_t>(kBandSplitDim) * kDim);
+    gam.resize(kBandSplitDim);
+    bias.resize(static_cast<size_t>(kBands) * kDim);
+    for (int b = 0; b < kBands; ++b) {
+      const int d = 4 * kBandFreqs[b];
+      unpack_packed(v.bw[b], d, kDim, w);  // w[n][k]
+      for (int k = 0; k < d; ++k)
+        for (int n = 0; n < kDim; ++n)
+          wt[static_cast<size_t>(wt_off[b]) + static_cast<size_t>(k) * kDim + n] = w[static_cast<size_t>(n) * d + k];
+      memcpy(&gam[g_off[b]], v.bg[b], d * 4);
+      memcpy(&bias[static_cast<size_t>(b) * kDim], v.bb[b], kDim * 4);
+    }
+  }
+  if (!upload_f32(g, arena, wt.data(), static_cast<size_t>(kBandSplitDim) * kDim, &out.wt) ||
+      !upload_f32(g, arena, gam.data(), kBandSplitDim, &out.gamma) ||
+      !upload_f32(g, arena, bias.data(), static_cast<size_t>(kBands) * kDim, &out.bias))
+    return false;
+  out.wt_off = static_cast<long long*>(arena.take(kBands * 8));
+  if (out.wt_off == nullptr || !put(g, arena, out.wt_off, wt_off.data(), kBands * 8, "band offsets")) return false;
+  out.gamma_off = static_cast<int*>(arena.take((kBands + 1) * 4));
+  return out.gamma_off != nullptr && put(g, arena, out.gamma_off, g_off.data(), (kBands + 1) * 4, "band offsets");
+}
+
+// ------------------------------------------------------------------ model image
+// The loaded model is one device allocation split into fixed regions: one per
+// axial block, then the band split, then the mask head.  A region is filled
+// by one task, so the tasks run on separate threads into a host image that
+// reaches the device in a single copy, and that image can be kept on disk.
+constexpr size_t round4k(size_t x) { return (x + 4095) & ~size_t(4095); }
+constexpr size_t kBandBytes = static_cast<size_t>(kBandSplitDim) * kDim * 4 + kBandSplitDim * 4 +
+                              static_cast<size_t>(kBands) * kDim * 4 + kBands * 8 + (kBands + 1) * 4 + 16 * 1024;
+constexpr size_t kBlockRegion = round4k(kBlockBytes);
+constexpr size_t kBandRegion = round4k(kBandBytes);
+constexpr size_t kMaskRegion = round4k(mask_bytes_estimate());
+constexpr int kMaskTasks = 6;   // the mask head's conversion is split by bands over this many tasks
+constexpr int kModelTasks = 2 * kDepth + 1 + kMaskTasks;
+constexpr size_t kModelBytes = 2 * kDepth * kBlockRegion + kBandRegion + kMaskRegion;
+
+size_t task_offset(int t) {
+  if (t < 2 * kDepth) return static_cast<size_t>(t) * kBlockRegion;
+  return 2 * kDepth * kBlockRegion + (t == 2 * kDepth ? 0 : kBandRegion);
+}
+size_t task_size(int t) { return t < 2 * kDepth ? kBlockRegion : (t == 2 * kDepth ? kBandRegion : kMaskRegion); }
+
+// Task t: axial block (t / 2, t % 2) for t < 32, 32 = band split, 33.. = mask
+// head, each of those converting a sixth of the bands in the same region.
+bool model_task(native_gpu* g, const PackView& v, int t, char* base, uint8_t* host, bool dry, bool maps,
+                BlockW (&blocks)[kDepth][2], BandW& band, MaskW& mask, uint64_t* layout) {
+  Arena a;
+  a.base = reinterpret_cast<char*>(reinterpret_cast<uintptr_t>(base) + task_offset(t));
+  a.cap = task_size(t);
+  a.host = host != nullptr ? host + task_offset(t) : nullptr;
+  a.dry = dry;
+  a.maps = maps;
+  bool ok;
+  if (t < 2 * kDepth)
+    ok = upload_block(g, a, v.layers[t / 2][t % 2], blocks[t / 2][t % 2]);
+  else if (t == 2 * kDepth)
+    ok = upload_band(g, a, v, band);
+  else {
+    const int k = t - (2 * kDepth + 1);
+    ok = upload_mask(g, a, v.mb, v.final_gamma, mask, kBands * k / kMaskTasks, kBands * (k + 1) / kMaskTasks, k == 0);
+  }
+  *layout = a.layout;
+  return ok;
+}
+
+uint64_t fold_layout(const uint64_t* h) {
+  uint64_t r = 1469598103934665603ull ^ kModelBytes;
+  for (int t = 0; t < kModelTasks; ++t) {
+    r = (r ^ h[t]) * 1099511628211ull;
+    r = (r ^ task_offset(t)) * 1099511628211ull;
+  }
+  return r;
+}
+
+// Nominal device base for host-only conversion: pointers there only locate
+// bytes in the image, and a null base would make the first one look like a
+// failed allocation.
+char* const kHostOnlyBase = reinterpret_cast<char*>(uintptr_t(1) << 20);
+
+int load_threads() {
+  const char* v = getenv("VOCALARC_B200_LOAD_THREADS");
+  if (v != nullptr && atoi(v) > 0) return atoi(v);
+  const unsigned n = std::thread::hardware_concurrency();
+  return n == 0 ? 4 : (n > 16 ? 16 : static_cast<int>(n));
+}
+
+// Converts every region into `image` (kModelBytes, zero-filled by the caller)
+// on `threads` threads; `layout` is the fold of the regions' layout hashes.
+bool build_image(native_gpu* g, const PackView& v, char* base, uint8_t* image, int threads, uint64_t* layout) {
+  uint64_t h[kModelTasks] = {};
+  // The mask head's tasks and the band split are the largest: start them first.
+  int order[kModelTasks];
+  int n_order = 0;
+  for (int t = 2 * kDepth + 1; t < kModelTasks; ++t) order[n_order++] = t;
+  order[n_order++] = 2 * kDepth;
+  for (int t = 0; t < 2 * kDepth; ++t) order[n_order++] = t;
+  std::atomic<int> next{0};
+  std::atomic<bool> ok{true};
+  auto worker = [&]() {
+    // Pointers land in scratch copies (equal to the layout pass's); no tensor maps.
+    std::vector<BlockW> scratch(2 * kDepth);
+    BlockW(*blocks)[kDepth][2] = reinterpret_cast<BlockW(*)[kDepth][2]>(scratch.data());
+    BandW band;
+    MaskW mask;
+    for (;;) {
+      const int i = next.fetch_add(1);
+      if (i >= kModelTasks) break;
+      const int t = order[i];
+      if (!model_task(g, v, t, base, image, false, false, *blocks, band, mask, &h[t])) ok = false;
+    }
+  };
+  const int n = threads < 1 ? 1 : (threads > kModelTasks ? kModelTasks : threads);
+  std::vector<std::thread> pool;
+  for (int i = 1; i < n; ++i) pool.emplace_back(worker);
+  worker();
+  for (auto& th : pool) th.join();
+  *layout = fold_layout(h);
+  return ok.load();
+}
+
+// 64-bit hash of the pack bytes (four interleaved multiply-xorshift lanes).
+uint64_t content_hash(const void* p, size_t n) {
+  const unsigned char* c = static_cast<const unsigned char*>(p);
+  uint64_t lane[4] = {0x9E3779B97F4A7C15ull ^ n, 0xC2B2AE3D27D4EB4Full, 0x165667B19E3779F9ull, 0xD6E8FEB86659FD93ull};
+  size_t i = 0;
+  for (; i + 32 <= n; i += 32)
+    for (int k = 0; k < 4; ++k) {
+      uint64_t w;
+      memcpy(&w, c + i + 8 * k, 8);
+      lane[k] = (lane[k] ^ w) * 0xFF51AFD7ED558CCDull;
+      lane[k] ^= lane[k] >> 29;
+    }
+  uint64_t h = lane[0] ^ (lane[1] * 31) ^ (lane[2] * 961) ^ (lane[3] * 29791);
+  for (; i < n; ++i) h = (h ^ c[i]) * 1099511628211ull;
+  h ^= h >> 33;
+  h *= 0xFF51AFD7ED558CCDull;
+  return h ^ (h >> 33);
+}
+
+// On-disk image: this header, then kModelBytes of the device arena.
+struct ImageHeader {
+  char magic[8];
+  uint64_t pack_hash;
+  uint64_t pack_bytes;
+  uint64_t layout_hash;
+  uint64_t image_bytes;
+  uint64_t image_hash;   // content_hash of the image bytes, checked before use
+  uint32_t bf16;
+  uint32_t reserved[3];
+};
+static_assert(sizeof(ImageHeader) == 64, "image header is 64 bytes");
+
+ImageHeader image_header(uint64_t pack_hash, size_t pack_bytes, uint64_t layout, int bf16) {
+  ImageHeader h;
+  memset(&h, 0, sizeof(h));
+  memcpy(h.magic, "VBIMG001", 8);
+  h.pack_hash = pack_hash;
+  h.pack_bytes = pack_bytes;
+  h.layout_hash = layout;
+  h.image_bytes = kModelBytes;
+  h.bf16 = bf16 ? 1u : 0u;
+  return h;
+}
+
+// Directory of converted images: VOCALARC_B200_IMAGE_CACHE ("off" disables),
+// else $XDG_CACHE_HOME/vocalarc-b200, else $HOME/.cache/vocalarc-b200.
+std::string image_cache_dir() {
+  const char* v = getenv("VOCALARC_B200_IMAGE_CACHE");
+  if (v != nullptr) {
+    if (*v == 0 || strcmp(v, "off") == 0 || strcmp(v, "0") == 0) return "";
+    return v;
+  }
+  const char* x = getenv("XDG_CACHE_HOME");
+  if (x != nullptr && *x != 0) return std::string(x) + "/vocalarc-b200";
+  const char* home = getenv("HOME");
+  if (home != nullptr && *home != 0) return std::string(home) + "/.cache/vocalarc-b200";
+  return "";
+}
+
+std::string image_path(const std::string& dir, const ImageHeader& h) {
+  char name[64];
+  snprintf(name, sizeof(name), "/%016llx.%s.vbimg", static_cast<unsigned long long>(h.pack_hash),
+           h.bf16 ? "bf16" : "fp16");
+  return dir + name;
+}
+
+bool make_dirs(const std::string& dir) {
+  for (size_t i = 1; i <= dir.size(); ++i) {
+    if (i == dir.size() || dir[i] == '/') {
+      const std::string part = dir.substr(0, i);
+      if (mkdir(part.c_str(), 0755) != 0 && errno != EEXIST) return false;
+    }
+  }
+  return true;
+}
+
+// The cached image at `path` when its header matches `want` (all but the
+// image hash) and its bytes hash to the recorded value; nullptr otherwise.
+const uint8_t* map_image(const std::string& path, const ImageHeader& want, size_t* mapped) {
+  const int fd = open(path.c_str(), O_RDONLY);
+  if (fd < 0) return nullptr;
+  struct stat st;
+  if (fstat(fd, &st) != 0 || static_cast<size_t>(st.st_size) != sizeof(ImageHeader) + want.image_bytes) {
+    close(fd);
+    return nullptr;
+  }
+  void* m = mmap(nullptr, static_cast<size_t>(st.st_size), PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (m == MAP_FAILED) return nullptr;
+  ImageHeader have;
+  memcpy(&have, m, sizeof(have));
+  ImageHeader expect = want;
+  expect.image_hash = have.image_hash;
+  if (memcmp(&have, &expect, sizeof(ImageHeader)) != 0 ||
+      content_hash(static_cast<const uint8_t*>(m) + sizeof(ImageHeader), want.image_bytes) != have.image_hash) {
+    munmap(m, static_cast<size_t>(st.st_size));
+    return nullptr;
+  }
+  *mapped = static_cast<size_t>(st.st_size);
+  return static_cast<const uint8_t*>(m);
+}
+
+// Writes the image next to its final name and renames it into place.
+bool store_image(const std::string& dir, ImageHeader h, const uint8_t* image) {
+  if (dir.empty() || !make_dirs(dir)) return false;
+  h.image_hash = content_hash(image, h.image_bytes);
+  const std::string path = image_path(dir, h);
+  const std::string tmp = path + ".tmp" + std::to_string(static_cast<long long>(getpid()));
+  FILE* f = fopen(tmp.c_str(), "wb");
+  if (f == nullptr) return false;
+  const bool ok = fwrite(&h, sizeof(h), 1, f) == 1 && fwrite(image, 1, h.image_bytes, f) == h.image_bytes;
+  if (fclose(f) != 0 || !ok || rename(tmp.c_str(), path.c_str()) != 0) {
+    unlink(tmp.c_str());
+    return false;
+  }
+  return true;
+}
+
 bool init_context(native_gpu* g, int device) {
   g->device = device;
   if (!cuda_ok(g, cudaSetDevice(device), "cudaSetDevice")) return false;
@@ -1023,98 +1397,97 @@ int native_gpu_resident_mask(native_gpu* g, int frames, const float* final_gamma
 int vocalarc_b200_load_model(native_gpu* g, const void* pack, size_t bytes) {
   if (!active(g) || pack == nullptr || bytes < 64) return 0;
   cudaSetDevice(g->device);
-  const unsigned char* base = static_cast<const unsigned char*>(pack);
-  uint32_t fields[14];
-  memcpy(fields, base + 8, sizeof(fields));
-  const uint32_t expect[12] = {1, kDim, kDepth, kBands, kHeads, kDimHead, kFreqBins, kChannels, kNfft, kHop, kNfft,
-                               kModelFrames};
-  if (memcmp(base, "VSCNAT01", 8) != 0 || memcmp(fields, expect, sizeof(expect)) != 0) {
-    fprintf(stderr, "vocalarc-b200: unsupported native model header\n");
-    return 0;
-  }
-  PackCursor cur{base + 64, base + bytes};
-  native_gpu_transformer_weights layers[kDepth][2];
-  for (int l = 0; l < kDepth; ++l)
-    for (int a = 0; a < 2; ++a) {
-      native_gpu_transformer_weights& w = layers[l][a];
-      w.gamma = cur.next(kDim);
-      w.qkv = cur.next(static_cast<uint64_t>(kQkvDim) * kDim);
-      w.gate_weight = cur.next(kHeads * kDim);
-      w.gate_bias = cur.next(kHeads);
-      w.out_weight = cur.next(static_cast<uint64_t>(kDim) * kDimInner);
-      w.ff_gamma = cur.next(kDim);
-      w.ff1_weight = cur.next(static_cast<uint64_t>(kFfDim) * kDim);
-      w.ff1_bias = cur.next(kFfDim);
-      w.ff2_weight = cur.next(static_cast<uint64_t>(kDim) * kFfDim);
-      w.ff2_bias = cur.next(kDim);
-      if (!w.gamma || !w.qkv || !w.gate_weight || !w.gate_bias || !w.out_weight || !w.ff_gamma || !w.ff1_weight ||
-          !w.ff1_bias || !w.ff2_weight || !w.ff2_bias) {
-        fprintf(stderr, "vocalarc-b200: native model truncated in layer %d\n", l);
-        return 0;
-      }
-    }
-  const float *bg[kBands], *bw[kBands], *bb[kBands];
-  for (int b = 0; b < kBands; ++b) {
-    const int d = 4 * kBandFreqs[b];
-    bg[b] = cur.next(d);
-    bw[b] = cur.next(static_cast<uint64_t>(kDim) * d);
-    bb[b] = cur.next(kDim);
-    if (!bg[b] || !bw[b] || !bb[b]) return 0;
-  }
-  const float* final_gamma = cur.next(kDim);
-  if (final_gamma == nullptr) return 0;
-  native_gpu_mask_band mb[kBands];
-  for (int b = 0; b < kBands; ++b) {
-    const int d = 4 * kBandFreqs[b];
-    mb[b].first_weight = cur.next(static_cast<uint64_t>(kFfDim) * kDim);
-    mb[b].first_bias = cur.next(kFfDim);
-    mb[b].second_weight = cur.next(static_cast<uint64_t>(2 * d) * kFfDim);
-    mb[b].second_bias = cur.next(2 * d);
-    mb[b].input_dim = d;
-    mb[b].first_frequency = band_first(b);
-    if (!mb[b].first_weight || !mb[b].first_bias || !mb[b].second_weight || !mb[b].second_bias) return 0;
-  }
+  PackView v;
+  if (!parse_pack_view(pack, bytes, v)) return 0;
   free_model(g);
-  const size_t band_bytes = static_cast<size_t>(kBandSplitDim) * kDim * 4 + kBandSplitDim * 4 + kBands * kDim * 4 +
-                            kBands * 8 + 91 * 4 + 16 * 1024;
-  const size_t total = 32 * kBlockBytes + mask_bytes_estimate() + band_bytes;
-  if (!cuda_ok(g, cudaMalloc(&g->model_mem, total), "cudaMalloc(model)")) return 0;
-  Arena arena{static_cast<char*>(g->model_mem), total, 0};
-  for (int l = 0; l < kDepth; ++l)
-    for (int a = 0; a < 2; ++a)
-      if (!upload_block(g, arena, layers[l][a], g->blocks[l][a])) return 0;
-  // Band split: W^T per band ([d_b][256]) for the SIMT kernel.
-  std::vector<float> wt(static_cast<size_t>(kBandSplitDim) * kDim), gam(kBandSplitDim), bias(kBands * kDim), w;
-  std::vector<long long> wt_off(kBands);
-  std::vector<int> g_off(kBands + 1);
-  size_t cur_wt = 0;
-  int cur_g = 0;
-  for (int b = 0; b < kBands; ++b) {
-    const int d = 4 * kBandFreqs[b];
-    unpack_packed(bw[b], d, kDim, w);  // w[n][k]
-    wt_off[b] = static_cast<long long>(cur_wt);
-    for (int k = 0; k < d; ++k)
-      for (int n = 0; n < kDim; ++n) wt[cur_wt + static_cast<size_t>(k) * kDim + n] = w[static_cast<size_t>(n) * d + k];
-    cur_wt += static_cast<size_t>(d) * kDim;
-    g_off[b] = cur_g;
-    memcpy(&gam[cur_g], bg[b], d * 4);
-    cur_g += d;
-    memcpy(&bias[static_cast<size_t>(b) * kDim], bb[b], kDim * 4);
+  if (!cuda_ok(g, cudaMalloc(&g->model_mem, kModelBytes), "cudaMalloc(model)")) return 0;
+  char* base = static_cast<char*>(g->model_mem);
+  // Layout pass: every device pointer and tensor map; no weight is touched.
+  uint64_t h[kModelTasks];
+  for (int t = 0; t < kModelTasks; ++t)
+    if (!model_task(g, v, t, base, nullptr, true, true, g->blocks, g->band, g->maskw, &h[t])) return 0;
+  const uint64_t layout = fold_layout(h);
+  const ImageHeader want = image_header(content_hash(pack, bytes), bytes, layout, g->bf16);
+  const std::string dir = image_cache_dir();
+  g->model_from_cache = 0;
+  size_t mapped = 0;
+  const uint8_t* cached = dir.empty() ? nullptr : map_image(image_path(dir, want), want, &mapped);
+  if (cached != nullptr) {
+    const bool ok = cuda_ok(g, cudaMemcpy(g->model_mem, cached + sizeof(ImageHeader), kModelBytes,
+                                          cudaMemcpyHostToDevice), "upload model image");
+    munmap(const_cast<uint8_t*>(cached), mapped);
+    if (!ok) return 0;
+    g->model_from_cache = 1;
+  } else {
+    std::vector<uint8_t> image(kModelBytes, 0);
+    uint64_t built = 0;
+    if (!build_image(g, v, base, image.data(), load_threads(), &built) || built != layout) {
+      fprintf(stderr, "vocalarc-b200: model conversion failed\n");
+      return 0;
+    }
+    if (!cuda_ok(g, cudaMemcpy(g->model_mem, image.data(), kModelBytes, cudaMemcpyHostToDevice), "upload model image"))
+      return 0;
+    if (!dir.empty() && !store_image(dir, want, image.data()))
+      fprintf(stderr, "vocalarc-b200: could not write the converted model to %s\n", dir.c_str());
   }
-  g_off[kBands] = cur_g;
-  if (!upload_f32(g, arena, wt.data(), wt.size(), &g->band.wt) ||
-      !upload_f32(g, arena, gam.data(), gam.size(), &g->band.gamma) ||
-      !upload_f32(g, arena, bias.data(), bias.size(), &g->band.bias))
-    return 0;
-  g->band.wt_off = static_cast<long long*>(arena.take(kBands * 8));
-  g->band.gamma_off = static_cast<int*>(arena.take((kBands + 1) * 4));
-  if (g->band.wt_off == nullptr || g->band.gamma_off == nullptr ||
-      !cuda_ok(g, cudaMemcpy(g->band.wt_off, wt_off.data(), kBands * 8, cudaMemcpyHostToDevice), "band offsets") ||
-      !cuda_ok(g, cudaMemcpy(g->band.gamma_off, g_off.data(), (kBands + 1) * 4, cudaMemcpyHostToDevice), "band offsets"))
-    return 0;
-  if (!upload_mask(g, arena, mb, final_gamma, g->maskw)) return 0;
   g->tiles_frames = 0;
   g->model_loaded = 1;
+  return 1;
+}
+
+int vocalarc_b200_load_model_file(native_gpu* g, const char* path) {
+  if (!active(g) || path == nullptr) return 0;
+  const int fd = open(path, O_RDONLY);
+  if (fd < 0) {
+    fprintf(stderr, "vocalarc-b200: cannot open %s\n", path);
+    return 0;
+  }
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size < 64) {
+    close(fd);
+    return 0;
+  }
+  void* m = mmap(nullptr, static_cast<size_t>(st.st_size), PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (m == MAP_FAILED) return 0;
+  const int ok = vocalarc_b200_load_model(g, m, static_cast<size_t>(st.st_size));
+  munmap(m, static_cast<size_t>(st.st_size));
+  return ok;
+}
+
+int vocalarc_b200_model_from_cache(const native_gpu* g) { return g != nullptr && g->model_loaded ? g->model_from_cache : 0; }
+
+int vocalarc_b200_model_image(const void* pack, size_t bytes, int bf16, int threads, void* out, size_t capacity,
+                              size_t* image_bytes) {
+  if (image_bytes != nullptr) *image_bytes = kModelBytes;
+  if (out == nullptr) return 1;
+  if (capacity < kModelBytes) return 0;
+  PackView v;
+  if (!parse_pack_view(pack, bytes, v)) return 0;
+  native_gpu host_only;   // conversion settings only; no CUDA call is made
+  host_only.bf16 = bf16 ? 1 : 0;
+  host_only.enabled = 1;
+  memset(out, 0, kModelBytes);
+  uint64_t layout = 0;
+  return build_image(&host_only, v, kHostOnlyBase, static_cast<uint8_t*>(out), threads > 0 ? threads : load_threads(),
+                     &layout)
+             ? 1
+             : 0;
+}
+
+int vocalarc_b200_store_model_image(const void* pack, size_t bytes, int bf16, char* path_out, int capacity) {
+  const std::string dir = image_cache_dir();
+  PackView v;
+  if (dir.empty() || !parse_pack_view(pack, bytes, v)) return 0;
+  native_gpu host_only;
+  host_only.bf16 = bf16 ? 1 : 0;
+  host_only.enabled = 1;
+  std::vector<uint8_t> image(kModelBytes, 0);
+  uint64_t layout = 0;
+  if (!build_image(&host_only, v, kHostOnlyBase, image.data(), load_threads(), &layout)) return 0;
+  const ImageHeader h = image_header(content_hash(pack, bytes), bytes, layout, host_only.bf16);
+  if (!store_image(dir, h, image.data())) return 0;
+  if (path_out != nullptr && capacity > 0) snprintf(path_out, static_cast<size_t>(capacity), "%s", image_path(dir, h).c_str());
   return 1;
 }
 

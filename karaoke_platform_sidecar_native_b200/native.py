@@ -60,6 +60,12 @@ _SIGNATURES = {
                                                 ctypes.c_int]),
     "vocalarc_b200_create": (_vp, [ctypes.c_int]),
     "vocalarc_b200_load_model": (ctypes.c_int, [_vp, ctypes.c_void_p, ctypes.c_size_t]),
+    "vocalarc_b200_load_model_file": (ctypes.c_int, [_vp, ctypes.c_char_p]),
+    "vocalarc_b200_model_from_cache": (ctypes.c_int, [_vp]),
+    "vocalarc_b200_model_image": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "vocalarc_b200_store_model_image": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                                       ctypes.c_char_p, ctypes.c_int]),
     "vocalarc_b200_separate": (ctypes.c_int, [_vp, _f32p, ctypes.c_int, _f32p]),
     "vocalarc_b200_separate_chunked": (ctypes.c_int, [_vp, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]),
     "vocalarc_b200_separate_device": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -104,6 +110,28 @@ def chunk_plan(length: int, chunk: int = 0) -> dict:
     if not lib.vocalarc_b200_chunk_plan(length, chunk, *[ctypes.byref(v) for v in vals]):
         raise ProviderError(f"chunk_plan({length}, {chunk}) failed")
     return dict(zip(("chunks", "step", "border", "seam"), (v.value for v in vals)))
+
+
+def model_image(blob: bytes, bf16: bool = False, threads: int = 0) -> np.ndarray:
+    """The converted device image of a VSCNAT01 pack, built on the host (no GPU)."""
+    lib = load()
+    size = ctypes.c_size_t(0)
+    lib.vocalarc_b200_model_image(None, 0, 0, 0, None, 0, ctypes.byref(size))
+    out = np.zeros(size.value, dtype=np.uint8)
+    ok = lib.vocalarc_b200_model_image(blob, len(blob), int(bf16), threads, out.ctypes.data_as(ctypes.c_void_p),
+                                       out.size, ctypes.byref(size))
+    if not ok:
+        raise ProviderError("vocalarc_b200_model_image failed")
+    return out
+
+
+def store_model_image(blob: bytes, bf16: bool = False) -> str:
+    """Convert a pack and write its image to the cache directory (no GPU); returns the file."""
+    lib = load()
+    path = ctypes.create_string_buffer(4096)
+    if not lib.vocalarc_b200_store_model_image(blob, len(blob), int(bf16), path, len(path)):
+        raise ProviderError("vocalarc_b200_store_model_image failed")
+    return path.value.decode()
 
 
 def declared_functions() -> list:
@@ -182,8 +210,15 @@ class Provider:
 
     # ---- extension -----------------------------------------------------
     def load_model(self, blob: bytes):
-        buf = ctypes.create_string_buffer(blob, len(blob))
-        self.check(self.lib.vocalarc_b200_load_model(self.handle, buf, len(blob)), "load_model")
+        # A bytes object is passed as a pointer to its own buffer (no copy).
+        self.check(self.lib.vocalarc_b200_load_model(self.handle, bytes(blob), len(blob)), "load_model")
+
+    def load_model_file(self, path: str):
+        self.check(self.lib.vocalarc_b200_load_model_file(self.handle, os.fsencode(path)), "load_model_file")
+
+    @property
+    def model_from_cache(self) -> bool:
+        return bool(self.lib.vocalarc_b200_model_from_cache(self.handle))
 
     def set_precision(self, bf16: bool):
         self.check(self.lib.vocalarc_b200_set_precision(self.handle, 1 if bf16 else 0), "set_precision")

@@ -13,6 +13,10 @@ from karaoke_platform_sidecar_native_b200 import modelpack  # noqa: E402
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
+    # Converted model images of this session go to a private directory, not ~/.cache.
+    if "VOCALARC_B200_IMAGE_CACHE" not in os.environ:
+        import tempfile
+        os.environ["VOCALARC_B200_IMAGE_CACHE"] = tempfile.mkdtemp(prefix="vocalarc_b200_images_")
 
 
 @pytest.fixture(scope="session")
