@@ -366,6 +366,7 @@ def main():
     e2e_value = world * args.seconds * e2e_steps / (e_ms / 1000.0)
     if not np.isfinite(out_np).all():
         raise RuntimeError("non-finite vocals")
+    latency = clip_latency(provider, stream) if rank == 0 else None
 
     if rank == 0:
         peaks = load_peaks()
@@ -418,6 +419,7 @@ def main():
                     "api": "vocalarc_b200_separate_chunked (C-ABI, pinned host buffers)"},
             "gpu_launches": int(launches),
             "model_load": model_load,
+            "latency_10s_clip": latency,
             "roofline": roofline,
             "kernels": kernels,
             "cpu_baseline": cpu,
@@ -429,6 +431,42 @@ def main():
         dist.destroy_process_group()
     provider.close()
     return 0
+
+
+def clip_latency(provider, stream, reps=20):
+    """p50 / p90 latency of one 10 s clip (config 1: seed-0 tone mix), whole-clip
+    forward (T = 862), 1 GPU: through the C-ABI call vocalarc_b200_separate
+    with host buffers (wall clock around the synchronous call) and on device
+    memory (CUDA events on the provider stream)."""
+    import torch
+
+    from karaoke_platform_sidecar_native_b200 import native
+
+    clip = np.ascontiguousarray(fixtures.tone_mix(seconds=10.0, seed=0), dtype=np.float32)
+    out = np.zeros_like(clip)
+    length = clip.shape[1]
+    d_clip = torch.from_numpy(clip).cuda()
+    d_out = torch.empty_like(d_clip)
+    for _ in range(3):
+        provider.lib.vocalarc_b200_separate(provider.handle, native.fptr(clip), length, native.fptr(out))
+    wall, dev = [], []
+    for _ in range(reps):
+        t = time.perf_counter()
+        if not provider.lib.vocalarc_b200_separate(provider.handle, native.fptr(clip), length, native.fptr(out)):
+            raise RuntimeError("vocalarc_b200_separate failed")
+        wall.append((time.perf_counter() - t) * 1000.0)
+    for _ in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        provider.separate_device(d_clip, 1, length, d_out)
+        b.record(stream)
+        torch.cuda.synchronize()
+        dev.append(a.elapsed_time(b))
+    q = lambda v, p: round(float(np.percentile(v, p)), 3)
+    return {"clip": "cfg1: 10 s stereo 44.1 kHz tone mix (seed 0), whole clip, T = 862", "reps": reps,
+            "e2e_ms_p50": q(wall, 50), "e2e_ms_p90": q(wall, 90), "device_ms_p50": q(dev, 50),
+            "device_ms_p90": q(dev, 90), "api": "vocalarc_b200_separate (host buffers, synchronous)"}
 
 
 def run_ops(args):

@@ -147,19 +147,14 @@ struct EpiWarp {
 // ---------------------------------------------------------------- 16-bit outputs
 // QKV (+RoPE, row scale), FF1 (+bias, GELU, row scale), plain store.  This warp
 // owns columns [128*half, 128*half + 128) of the tile in two 64-column steps.
+// `inv` and `rope` (this row's RMSNorm factor and RoPE cos/sin) are loaded by
+// the caller before it waits for the accumulator, so their latency overlaps
+// the MMA of the tile.
 template <typename T, int EPI>
 __device__ __forceinline__ void epilogue_out16(const GemmArgs& args, const CUtensorMap* map_out, const TileInfo& ti,
-                                               EpiWarp& ew, uint32_t taddr, int half, int row, long long R, bool valid,
-                                               int row0) {
-  const float inv = (args.row_inv != nullptr && valid) ? __ldg(args.row_inv + R) : 1.0f;
-  float4 rope[16];
+                                               EpiWarp& ew, uint32_t taddr, int half, int row, int row0, float inv,
+                                               const float4 (&rope)[16]) {
   const bool do_rope = EPI == kEpiQkvRope && ti.n0 < args.rope_cols;
-  if (EPI == kEpiQkvRope) {
-    const int pos = static_cast<int>((R / args.pos_div) % args.pos_mod);
-    const float4* table = reinterpret_cast<const float4*>(args.rope + static_cast<long long>(pos) * (kDimHead / 2));
-#pragma unroll
-    for (int i = 0; i < 16; ++i) rope[i] = (valid && do_rope) ? __ldg(table + i) : make_float4(1.f, 0.f, 1.f, 0.f);
-  }
 #pragma unroll
   for (int s = 0; s < 2; ++s) {
     const int c = half * 128 + s * 64;   // tile column of this step
@@ -344,9 +339,7 @@ __device__ __forceinline__ void epilogue_residual(const GemmArgs& args, const CU
 // and written by one TMA store at output column (n0 + 128 half) / 2.
 template <typename T>
 __device__ __forceinline__ void epilogue_geglu(const GemmArgs& args, const CUtensorMap* map_out, const TileInfo& ti,
-                                               EpiWarp& ew, uint32_t taddr, int half, int row, long long R, bool valid,
-                                               int row0) {
-  const float inv = (args.row_inv != nullptr && valid) ? __ldg(args.row_inv + R) : 1.0f;
+                                               EpiWarp& ew, uint32_t taddr, int half, int row, int row0, float inv) {
   const float2 inv2 = make_float2(inv, inv);
   uint8_t* buf = ew.buf[ew.cur];
   if (ew.lane == 0) bulk_wait_read1();   // the store that last used this buffer has read it
@@ -394,8 +387,7 @@ __device__ __forceinline__ void epilogue_geglu(const GemmArgs& args, const CUten
 // Grouped mask layers, the QKV gate tile and the fp32 test store.
 template <typename T, int EPI>
 __device__ __forceinline__ void epilogue_direct(const GemmArgs& args, const TileInfo& ti, uint32_t taddr, int half,
-                                                long long R, bool valid) {
-  const float inv = (args.row_inv != nullptr && valid) ? __ldg(args.row_inv + R) : 1.0f;
+                                                long long R, bool valid, float inv) {
   const int c_end = min(ti.n_size, half * 128 + 128);
   for (int c = half * 128; c < c_end; c += 32) {
     float v[32];
@@ -643,21 +635,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
-      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, args.err, kErrWaitEpilogue)) break;
-      tc_fence_after();
+      // Row values that do not depend on the accumulator are loaded before
+      // the wait, while the tile's MMAs run.
       const TileInfo ti = decode_tile(args, tile);
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
       const long long R = static_cast<long long>(ti.a_row) + row;
       const bool valid = row < ti.m_valid;
+      const float inv = (EPI != kEpiResidual && args.row_inv != nullptr && valid) ? __ldg(args.row_inv + R) : 1.0f;
+      float4 rope[16];
+      if (EPI == kEpiQkvRope) {
+        const bool do_rope = valid && ti.n_size == kBN && ti.n0 < args.rope_cols;
+        const int pos = static_cast<int>((R / args.pos_div) % args.pos_mod);
+        const float4* table = reinterpret_cast<const float4*>(args.rope + static_cast<long long>(pos) * (kDimHead / 2));
+#pragma unroll
+        for (int i = 0; i < 16; ++i) rope[i] = do_rope ? __ldg(table + i) : make_float4(1.f, 0.f, 1.f, 0.f);
+      }
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, args.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
       const int row0 = ti.a_row + quarter * 32;
       if (EPI == kEpiResidual) {
         epilogue_residual<T>(args, &map_c, &map_d, ti, ew, taddr, half, quarter, row, R, valid, row0, it & 1, red);
       } else if (EPI == kEpiGeglu) {
-        epilogue_geglu<T>(args, &map_c, ti, ew, taddr, half, row, R, valid, row0);
+        epilogue_geglu<T>(args, &map_c, ti, ew, taddr, half, row, row0, inv);
       } else if ((EPI == kEpiStore || EPI == kEpiGelu || EPI == kEpiQkvRope) && ti.n_size == kBN) {
-        epilogue_out16<T, EPI>(args, &map_c, ti, ew, taddr, half, row, R, valid, row0);
+        epilogue_out16<T, EPI>(args, &map_c, ti, ew, taddr, half, row, row0, inv, rope);
       } else {
-        epilogue_direct<T, EPI>(args, ti, taddr, half, R, valid);
+        epilogue_direct<T, EPI>(args, ti, taddr, half, R, valid, inv);
       }
       tc_fence_before();
       __syncwarp();
