@@ -250,6 +250,7 @@ def main():
     parser.add_argument("--cpu-sample-seconds", type=float, default=2.0)
     parser.add_argument("--reference-sample-seconds", type=float, default=1.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-latency", action="store_true", help="skip the 10 s clip latency measurement")
     parser.add_argument("--precision", default="fp16", choices=("fp16", "bf16"))
     parser.add_argument("--ops", action="store_true",
                         help="config-4 op-level lines: time/band attention, STFT, band split")
@@ -366,7 +367,7 @@ def main():
     e2e_value = world * args.seconds * e2e_steps / (e_ms / 1000.0)
     if not np.isfinite(out_np).all():
         raise RuntimeError("non-finite vocals")
-    latency = clip_latency(provider, stream) if rank == 0 else None
+    latency = clip_latency(provider, stream) if rank == 0 and not args.no_latency else None
 
     if rank == 0:
         peaks = load_peaks()
