@@ -1,6 +1,6 @@
 """Generate golden fixtures from the UNCHANGED reference CPU executable.
 
-Run in the build container (needs ``/root/reference`` and ``make -C oracle ref``):
+Run where the reference sources are checked out (``make -C oracle ref REF=<reference>/native``):
 
     python tests/golden/make_golden.py
 

@@ -1,7 +1,7 @@
 """The CPU oracle pinned against the reference executable's own outputs.
 
 The golden fixtures come from the unchanged reference CPU build
-(tests/golden/make_golden.py); these tests need no GPU and no /root/reference.
+(tests/golden/make_golden.py); these tests need no GPU and no checkout of the reference.
 """
 
 import os
