@@ -258,6 +258,8 @@ def main():
                         help="strong scaling: one track's chunks sharded across the ranks, seams by CUDA IPC")
     parser.add_argument("--stack", action="store_true",
                         help="config 3: dim-512 / 62-band / hop-441 / GEGLU stack, 16 x 8 s clips, bf16")
+    parser.add_argument("--sp", action="store_true",
+                        help="10 s clip latency with the clip split across every visible GPU (one process)")
     parser.add_argument("--clips", type=int, default=0, help="--stack: clips per forward (default 16)")
     parser.add_argument("--depth", type=int, default=0, help="--stack: layers (default 12; fewer for profiling)")
     args = parser.parse_args()
@@ -274,6 +276,8 @@ def main():
         return run_ops(args)
     if args.stack:
         return run_stack(args)
+    if args.sp:
+        return run_sp(args)
 
     import torch
     import torch.distributed as dist
@@ -641,6 +645,51 @@ def run_stack(args):
     }
     print(json.dumps(line), flush=True)
     s.close()
+    return 0
+
+
+def run_sp(args, reps=20):
+    """Latency of one 10 s clip (config 1, seed 0, whole clip) with its forward
+    split across all visible GPUs by vocalarc_b200_separate_sp (time-axis
+    blocks on band ranges, band-axis blocks on frame ranges), against the same
+    clip on GPU 0 alone.  One process drives every GPU; wall clock around the
+    synchronous C-ABI calls, host buffers."""
+    import torch
+
+    from karaoke_platform_sidecar_native_b200 import native
+
+    n = torch.cuda.device_count()
+    pack = modelpack.synthetic_pack(**modelpack.BENCH_RECIPE)
+    providers = []
+    for d in range(n):
+        p = native.Provider(d)
+        p.load_model(pack)
+        providers.append(p)
+    clip = np.ascontiguousarray(fixtures.tone_mix(seconds=10.0, seed=0), dtype=np.float32)
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        out = []
+        for _ in range(reps):
+            t = time.perf_counter()
+            fn()
+            out.append((time.perf_counter() - t) * 1000.0)
+        return round(float(np.percentile(out, 50)), 3), round(float(np.percentile(out, 90)), 3)
+
+    one = timed(lambda: providers[0].separate(clip))
+    split = timed(lambda: native.separate_sp(providers, clip))
+    same = bool(np.array_equal(native.separate_sp(providers, clip), providers[0].separate(clip)))
+    print(json.dumps({"metric": "p50 latency of one 10 s clip, whole-clip forward split across GPUs",
+                      "unit": "ms", "n_gpus": n, "higher_is_better": False, "data": "synthetic",
+                      "split_ms_p50": split[0], "split_ms_p90": split[1], "one_gpu_ms_p50": one[0],
+                      "one_gpu_ms_p90": one[1], "bit_identical_to_one_gpu": same, "reps": reps,
+                      "config": {"workload": "cfg1: 10 s stereo 44.1 kHz tone mix (seed 0), T = 862, bundled-layout "
+                                             "model, synthetic N(0,0.02) weights",
+                                 "api": "vocalarc_b200_separate_sp vs vocalarc_b200_separate (host buffers)"}}),
+          flush=True)
+    for p in providers:
+        p.close()
     return 0
 
 

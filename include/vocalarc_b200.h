@@ -68,6 +68,23 @@ int vocalarc_b200_separate_chunked(native_gpu *gpu, const float *audio, int leng
 int vocalarc_b200_separate_tta(native_gpu *gpu, const float *audio, int length, int chunk_samples,
                                int model_batch, int bigshifts, int tta, float *vocals);
 
+/* One clip's whole-clip forward split across `count` providers, normally one
+   per GPU of one node, for the latency of a single clip (sequence parallelism;
+   no counterpart in the reference).  Each provider must have the model loaded.
+   Provider r runs the time-axis blocks for bands [90 r/count, 90 (r+1)/count)
+   and the band-axis blocks for frames [T r/count, T (r+1)/count); between the
+   axes the rows cross by 2-D peer copies ordered with CUDA events (x, its
+   16-bit copy and the row RMSNorm factor), so the result equals
+   vocalarc_b200_separate on provider 0 bit for bit.  Provider 0 runs the STFT,
+   band split, mask head and iSTFT.  Host buffers; returns when vocals is
+   written.  sp_plan lists the copies of one exchange (phase 0: scatter from
+   provider 0, 1: band to frame ranges, 2: frame to band ranges, 3: gather to
+   provider 0) as 8 values each: source, destination, source row, source pitch,
+   destination row, destination pitch, width, height (in token rows); it
+   returns the count, or -1. */
+int vocalarc_b200_separate_sp(native_gpu *const *gpus, int count, const float *audio, int length, float *vocals);
+int vocalarc_b200_sp_plan(int count, int frames, int phase, long long *out, int capacity);
+
 /* Device-pointer variants on the provider's stream; they return after
    enqueueing (call vocalarc_b200_synchronize).  `tracks` planar clips of
    `length` samples each are laid out back to back ([tracks][2][length]). */

@@ -12,6 +12,7 @@
 // band-major rows directly as its per-band A operand.  Every RMSNorm gamma is
 // folded into the weights of the GEMM that consumes the norm, and the GEMM
 // that updates x writes the per-row factor sqrt(256)/|x| next to x16.
+#include <algorithm>
 #include <atomic>
 #include <cerrno>
 #include <cmath>
@@ -184,6 +185,10 @@ struct native_gpu {
   long long ws_tokens = 0;
   float* x = nullptr;
   float* x_alt = nullptr;
+  void* x16_alt = nullptr;      // sequence parallelism: incoming copies of x16 / row_inv
+  float* row_inv_alt = nullptr;
+  long long sp_tokens = 0;
+  int sp_parity = 0;            // x / x16 / row_inv and their alternates are swapped
   void* x16 = nullptr;          // 16-bit copy of x (A operand of the norm-folded GEMMs)
   float* row_inv = nullptr;     // per-row sqrt(256)/|x| of the current x
   int stats_valid = 0;          // x16 / row_inv describe the current x
@@ -788,6 +793,118 @@ bool separate_device_impl(native_gpu* g, const float* d_audio, int tracks, int l
   return true;
 }
 
+// ------------------------------------------------------------------ sequence parallelism
+// One clip's whole-clip forward split across providers (one per GPU): rank r
+// holds the band range [kBands r / n, kBands (r + 1) / n) over all T frames for
+// the time-axis blocks (band-major [nb][T] rows), and the frame range
+// [T s / n, T (s + 1) / n) over all 90 bands for the band-axis blocks
+// ([90][nf] rows).  Between axes every rank copies to every other the rows the
+// other needs -- x, its 16-bit copy and the row RMSNorm factor, so the row
+// statistics stay valid and every row sees exactly the arithmetic of the
+// single-GPU forward.  A copy is one 2-D block (rows of one band are
+// contiguous in both layouts).
+struct SpCopy {
+  int src, dst;
+  long long src_row, src_pitch, dst_row, dst_pitch, width, height;   // in token rows
+};
+
+int sp_band_lo(int r, int n) { return kBands * r / n; }
+int sp_frame_lo(int r, int n, int frames) { return static_cast<int>(static_cast<long long>(frames) * r / n); }
+
+// Phase 0: rank 0's full band-major x to the other ranks' band ranges.
+// Phase 1: band ranges -> frame ranges.  Phase 2: frame ranges -> band ranges.
+// Phase 3: frame ranges -> rank 0's full band-major x.
+std::vector<SpCopy> sp_plan(int n, int frames, int phase) {
+  std::vector<SpCopy> plan;
+  const long long t = frames;
+  for (int d = 0; d < n; ++d)
+    for (int r = 0; r < n; ++r) {
+      const long long nb_d = sp_band_lo(d + 1, n) - sp_band_lo(d, n), nb_r = sp_band_lo(r + 1, n) - sp_band_lo(r, n);
+      const long long nf_d = sp_frame_lo(d + 1, n, frames) - sp_frame_lo(d, n, frames);
+      const long long nf_r = sp_frame_lo(r + 1, n, frames) - sp_frame_lo(r, n, frames);
+      SpCopy c{r, d, 0, 0, 0, 0, 0, 0};
+      if (phase == 0) {
+        if (r != 0 || d == 0) continue;
+        c = SpCopy{0, d, sp_band_lo(d, n) * t, nb_d * t, 0, nb_d * t, nb_d * t, 1};
+      } else if (phase == 1) {
+        c = SpCopy{r, d, sp_frame_lo(d, n, frames), t, sp_band_lo(r, n) * nf_d, nf_d, nf_d, nb_r};
+      } else if (phase == 2) {
+        c = SpCopy{r, d, sp_band_lo(d, n) * nf_r, nf_r, sp_frame_lo(r, n, frames), t, nf_r, nb_d};
+      } else {
+        if (d != 0) continue;
+        c = SpCopy{r, 0, 0, nf_r, sp_frame_lo(r, n, frames), t, nf_r, kBands};
+      }
+      if (c.width > 0 && c.height > 0) plan.push_back(c);
+    }
+  return plan;
+}
+
+void sp_swap(native_gpu* g) {
+  std::swap(g->x, g->x_alt);
+  std::swap(g->x16, g->x16_alt);
+  std::swap(g->row_inv, g->row_inv_alt);
+  g->sp_parity ^= 1;
+}
+
+// Workspace for rows of every layout plus the alternates the copies land in.
+bool ensure_sp(native_gpu* g, long long tokens) {
+  if (g->sp_parity) sp_swap(g);
+  if (!ensure_tokens(g, tokens)) return false;
+  if (tokens <= g->sp_tokens) return true;
+  g->sp_tokens = 0;
+  if (!grow(g, &g->x16_alt, static_cast<size_t>(tokens) * kDim * 2, "cudaMalloc(x16_alt)") ||
+      !grow(g, &g->row_inv_alt, static_cast<size_t>(tokens) * 4, "cudaMalloc(row_inv_alt)"))
+    return false;
+  g->sp_tokens = tokens;
+  return true;
+}
+
+// One exchange: each destination's stream waits for every source's last
+// block (ev), then copies x, x16 and row_inv.  Phase 0 writes straight into
+// the destination's buffers; the others write into its alternates, which it
+// then swaps in.  Source pointers are taken before any swap of this phase.
+bool sp_exchange(native_gpu* const* gpus, int n, int frames, int phase, const std::vector<cudaEvent_t>& ev) {
+  std::vector<float*> sx(n), sinv(n);
+  std::vector<char*> s16(n);
+  for (int r = 0; r < n; ++r) {
+    sx[r] = gpus[r]->x;
+    s16[r] = static_cast<char*>(gpus[r]->x16);
+    sinv[r] = gpus[r]->row_inv;
+  }
+  const std::vector<SpCopy> plan = sp_plan(n, frames, phase);
+  for (int d = 0; d < n; ++d) {
+    native_gpu* g = gpus[d];
+    bool any = false;
+    for (const SpCopy& c : plan) any = any || c.dst == d;
+    if (!any) continue;
+    cudaSetDevice(g->device);
+    for (int r = 0; r < n; ++r)
+      if (r != d && !cuda_ok(g, cudaStreamWaitEvent(g->stream, ev[r], 0), "exchange wait")) return false;
+    float* dx = phase == 0 ? g->x : g->x_alt;
+    char* d16 = static_cast<char*>(phase == 0 ? g->x16 : g->x16_alt);
+    float* dinv = phase == 0 ? g->row_inv : g->row_inv_alt;
+    for (const SpCopy& c : plan) {
+      if (c.dst != d) continue;
+      const size_t rx = kDim * 4, r16 = kDim * 2, ri = 4;
+      if (!cuda_ok(g, cudaMemcpy2DAsync(reinterpret_cast<char*>(dx) + c.dst_row * rx, c.dst_pitch * rx,
+                                        reinterpret_cast<const char*>(sx[c.src]) + c.src_row * rx, c.src_pitch * rx,
+                                        c.width * rx, c.height, cudaMemcpyDefault, g->stream),
+                   "exchange x") ||
+          !cuda_ok(g, cudaMemcpy2DAsync(d16 + c.dst_row * r16, c.dst_pitch * r16, s16[c.src] + c.src_row * r16,
+                                        c.src_pitch * r16, c.width * r16, c.height, cudaMemcpyDefault, g->stream),
+                   "exchange x16") ||
+          !cuda_ok(g, cudaMemcpy2DAsync(reinterpret_cast<char*>(dinv) + c.dst_row * ri, c.dst_pitch * ri,
+                                        reinterpret_cast<const char*>(sinv[c.src]) + c.src_row * ri,
+                                        c.src_pitch * ri, c.width * ri, c.height, cudaMemcpyDefault, g->stream),
+                   "exchange row factor"))
+        return false;
+    }
+    if (phase != 0) sp_swap(g);
+    g->stats_valid = 1;
+  }
+  return true;
+}
+
 struct PackCursor {
   const unsigned char* p;
   const unsigned char* end;
@@ -1237,7 +1354,8 @@ void native_gpu_destroy(native_gpu* g) {
   if (g->stream != nullptr) cudaStreamSynchronize(g->stream);
   void* ptrs[] = {g->x, g->x_alt, g->x16, g->row_inv, g->qkv, g->attn, g->gates, g->spec, g->mask, g->frames_buf,
                   g->seg_out, g->audio_in, g->audio_out, g->d_tiles1, g->d_tiles2, g->d_err, g->d_window,
-                  g->d_twiddle, g->d_rope, g->abi_mask_mem, g->seam_out, g->seam_in, g->tta_in, g->tta_out};
+                  g->d_twiddle, g->d_rope, g->abi_mask_mem, g->seam_out, g->seam_in, g->tta_in, g->tta_out,
+                  g->x16_alt, g->row_inv_alt};
   for (void* p : ptrs)
     if (p != nullptr) cudaFree(p);
   for (auto& e : g->block_cache) cudaFree(e.mem);
@@ -1525,6 +1643,125 @@ int vocalarc_b200_separate(native_gpu* g, const float* audio, int length, float*
 int vocalarc_b200_separate_chunked(native_gpu* g, const float* audio, int length, int chunk_samples, int model_batch,
                                    float* vocals) {
   return separate_host(g, audio, length, 1, chunk_samples, model_batch, vocals);
+}
+
+// ------------------------------------------------------------------ sequence parallelism
+int vocalarc_b200_sp_plan(int count, int frames, int phase, long long* out, int capacity) {
+  if (count < 1 || count > kBands || frames < count || phase < 0 || phase > 3) return -1;
+  const std::vector<SpCopy> plan = sp_plan(count, frames, phase);
+  if (out != nullptr) {
+    if (capacity < static_cast<int>(plan.size())) return -1;
+    for (size_t i = 0; i < plan.size(); ++i) {
+      const SpCopy& c = plan[i];
+      const long long v[8] = {c.src, c.dst, c.src_row, c.src_pitch, c.dst_row, c.dst_pitch, c.width, c.height};
+      memcpy(out + 8 * i, v, sizeof(v));
+    }
+  }
+  return static_cast<int>(plan.size());
+}
+
+int vocalarc_b200_separate_sp(native_gpu* const* gpus, int count, const float* audio, int length, float* vocals) {
+  if (gpus == nullptr || count < 1 || count > kBands || audio == nullptr || vocals == nullptr || length <= 0) return 0;
+  const int frames = length / kHop + 1;
+  if (frames < count) {
+    fprintf(stderr, "vocalarc-b200: %d frames cannot be split over %d providers\n", frames, count);
+    return 0;
+  }
+  for (int r = 0; r < count; ++r) {
+    if (!active(gpus[r]) || !gpus[r]->model_loaded || gpus[r]->bf16 != gpus[0]->bf16 || gpus[r]->resident_active) {
+      fprintf(stderr, "vocalarc-b200: provider %d of the split is not ready (model, precision or open session)\n", r);
+      return 0;
+    }
+    for (int q = 0; q < r; ++q)
+      if (gpus[q] == gpus[r]) return 0;
+  }
+  native_gpu* g0 = gpus[0];
+  const long long full = static_cast<long long>(kBands) * frames;
+  // Every allocation happens before any work is queued.
+  for (int r = 0; r < count; ++r) {
+    native_gpu* g = gpus[r];
+    cudaSetDevice(g->device);
+    if (!ensure_sp(g, full) || !ensure_rope(g, frames > kBands ? frames : kBands)) return 0;
+    for (int q = 0; q < count; ++q) {
+      if (gpus[q]->device == g->device) continue;
+      int can = 0;
+      // Direct peer reads where the pair supports them (an already enabled pair
+      // reports an error that is cleared here, as is any refusal: the copies
+      // then go through the host).
+      if (cudaDeviceCanAccessPeer(&can, g->device, gpus[q]->device) == cudaSuccess && can)
+        cudaDeviceEnablePeerAccess(gpus[q]->device, 0);
+      cudaGetLastError();
+    }
+  }
+  cudaSetDevice(g0->device);
+  if (!ensure_frames(g0, frames) || !ensure_audio(g0, 2ll * length) || !ensure_mask_tiles(g0, frames, g0->maskw))
+    return 0;
+  std::vector<cudaEvent_t> ev(count, nullptr);
+  bool ok = true;
+  for (int r = 0; r < count && ok; ++r) {
+    cudaSetDevice(gpus[r]->device);
+    ok = cuda_ok(gpus[r], cudaEventCreateWithFlags(&ev[r], cudaEventDisableTiming), "cudaEventCreate");
+  }
+  auto record = [&](int r) {
+    cudaSetDevice(gpus[r]->device);
+    return cuda_ok(gpus[r], cudaEventRecord(ev[r], gpus[r]->stream), "cudaEventRecord");
+  };
+  // Front end on rank 0: STFT, band split and row statistics of the whole clip.
+  if (ok) {
+    cudaSetDevice(g0->device);
+    ok = cuda_ok(g0, cudaMemcpyAsync(g0->audio_in, audio, 2ll * length * 4, cudaMemcpyHostToDevice, g0->stream),
+                 "H2D audio") &&
+         launched(g0, launch_stft(g0->audio_in, whole_clip_map(length), 1, frames, g0->d_window, g0->d_twiddle,
+                                  g0->spec, g0->stream),
+                  "stft") &&
+         launched(g0, launch_band_split(g0->spec, 1, frames, g0->band.wt, g0->band.wt_off, g0->band.gamma,
+                                        g0->band.gamma_off, g0->band.bias, g0->x, g0->stream),
+                  "band split");
+    g0->stats_valid = 0;
+    ok = ok && ensure_stats(g0, full) && record(0) && sp_exchange(gpus, count, frames, 0, ev);
+  }
+  for (int layer = 0; layer < kDepth && ok; ++layer) {
+    for (int r = 0; r < count && ok; ++r) {   // time axis on band ranges
+      native_gpu* g = gpus[r];
+      const int nb = sp_band_lo(r + 1, count) - sp_band_lo(r, count);
+      cudaSetDevice(g->device);
+      ok = run_block(g, g->blocks[layer][0], static_cast<long long>(nb) * frames,
+                     AxisPlan{1, frames, nb, 1, nb, frames, 1, frames}) &&
+           record(r);
+    }
+    ok = ok && sp_exchange(gpus, count, frames, 1, ev);
+    for (int r = 0; r < count && ok; ++r) {   // band axis on frame ranges
+      native_gpu* g = gpus[r];
+      const int nf = sp_frame_lo(r + 1, count, frames) - sp_frame_lo(r, count, frames);
+      cudaSetDevice(g->device);
+      ok = run_block(g, g->blocks[layer][1], static_cast<long long>(kBands) * nf,
+                     AxisPlan{2, nf, kBands, 1, nf, kBands, nf, kBands}) &&
+           record(r);
+    }
+    ok = ok && sp_exchange(gpus, count, frames, layer + 1 < kDepth ? 2 : 3, ev);
+  }
+  // Mask head and iSTFT on rank 0.
+  if (ok) {
+    cudaSetDevice(g0->device);
+    ok = run_mask(g0, g0->maskw, 1, frames, false, false, g0->mask) &&
+         launched(g0, launch_istft_frames(g0->spec, g0->mask, 1, frames, g0->d_window, g0->d_twiddle, g0->frames_buf,
+                                          g0->stream),
+                  "istft") &&
+         launched(g0, launch_overlap_add(g0->frames_buf, 1, frames, length, g0->d_window, g0->audio_out, g0->stream),
+                  "overlap-add") &&
+         cuda_ok(g0, cudaMemcpyAsync(vocals, g0->audio_out, 2ll * length * 4, cudaMemcpyDeviceToHost, g0->stream),
+                 "D2H vocals");
+  }
+  // Every stream drains (also on failure) before the buffers are put back in order.
+  for (int r = 0; r < count; ++r) {
+    native_gpu* g = gpus[r];
+    cudaSetDevice(g->device);
+    if (!sync_and_check(g, "separate_sp")) ok = false;
+    if (g->sp_parity) sp_swap(g);
+    g->stats_valid = 0;
+    if (ev[r] != nullptr) cudaEventDestroy(ev[r]);
+  }
+  return ok ? 1 : 0;
 }
 
 // ------------------------------------------------------------------ chunk ranges

@@ -71,6 +71,10 @@ _SIGNATURES = {
     "vocalarc_b200_separate_device": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                      ctypes.c_int, ctypes.c_int, _vp]),
     "vocalarc_b200_synchronize": (ctypes.c_int, [_vp]),
+    "vocalarc_b200_separate_sp": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _f32p, ctypes.c_int,
+                                                 _f32p]),
+    "vocalarc_b200_sp_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.POINTER(ctypes.c_longlong), ctypes.c_int]),
     "vocalarc_b200_stream": (_vp, [_vp]),
     "vocalarc_b200_take_device_error": (ctypes.c_int, [_vp]),
     "vocalarc_b200_set_precision": (ctypes.c_int, [_vp, ctypes.c_int]),
@@ -110,6 +114,29 @@ def chunk_plan(length: int, chunk: int = 0) -> dict:
     if not lib.vocalarc_b200_chunk_plan(length, chunk, *[ctypes.byref(v) for v in vals]):
         raise ProviderError(f"chunk_plan({length}, {chunk}) failed")
     return dict(zip(("chunks", "step", "border", "seam"), (v.value for v in vals)))
+
+
+def sp_plan(count: int, frames: int, phase: int) -> np.ndarray:
+    """Copies of one sequence-parallel exchange: rows of (src, dst, src_row, src_pitch,
+    dst_row, dst_pitch, width, height), in token rows."""
+    lib = load()
+    n = lib.vocalarc_b200_sp_plan(count, frames, phase, None, 0)
+    if n < 0:
+        raise ProviderError(f"sp_plan({count}, {frames}, {phase}) rejected")
+    out = np.zeros((max(n, 1), 8), dtype=np.int64)
+    lib.vocalarc_b200_sp_plan(count, frames, phase, out.ctypes.data_as(ctypes.POINTER(ctypes.c_longlong)), n)
+    return out[:n]
+
+
+def separate_sp(providers: list, audio: np.ndarray) -> np.ndarray:
+    """One clip's whole-clip forward split across the providers (one per GPU)."""
+    lib = load()
+    audio = np.ascontiguousarray(audio, dtype=np.float32)
+    out = np.zeros_like(audio)
+    handles = (ctypes.c_void_p * len(providers))(*[p.handle for p in providers])
+    if not lib.vocalarc_b200_separate_sp(handles, len(providers), fptr(audio), audio.shape[1], fptr(out)):
+        raise ProviderError("vocalarc_b200_separate_sp failed")
+    return out
 
 
 def model_image(blob: bytes, bf16: bool = False, threads: int = 0) -> np.ndarray:
