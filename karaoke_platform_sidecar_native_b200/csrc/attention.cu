@@ -524,13 +524,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
 template <typename T>
 cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, int sm_count, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PairSmem::kBytes);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  const cudaError_t e = opt_in_smem(attention_pair_kernel<T>, PairSmem::kBytes, configured);
+  if (e != cudaSuccess) return e;
   const long long units = static_cast<long long>((args.q_tiles + 1) / 2) * kHeads * args.sequences;
   if (units <= 0) return cudaSuccess;
   const int grid = units < sm_count ? static_cast<int>(units) : sm_count;
@@ -958,13 +954,9 @@ __global__ void __launch_bounds__(kItemThreads, 1)
 
 template <typename T, int NCOLS>
 cudaError_t launch_items_cols(const CUtensorMap& map, const AttnArgs& args, int sm_count, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_items_kernel<T, NCOLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         ItemSmem::kBytes);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  const cudaError_t e = opt_in_smem(attention_items_kernel<T, NCOLS>, ItemSmem::kBytes, configured);
+  if (e != cudaSuccess) return e;
   const long long items = static_cast<long long>(args.sequences) * kHeads;
   if (items <= 0) return cudaSuccess;
   // Gated output [rows][512] viewed like the qkv map: (512, d1, d2, d3), one

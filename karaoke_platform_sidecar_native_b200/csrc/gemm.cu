@@ -680,12 +680,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <typename T, int EPI>
 cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& args, int sm_count, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  const cudaError_t e = opt_in_smem(gemm_kernel<T, EPI>, kSmemBytes, configured);
+  if (e != cudaSuccess) return e;
   if (args.num_tiles <= 0) return cudaSuccess;
   const int grid = args.num_tiles < sm_count ? args.num_tiles : sm_count;
   gemm_kernel<T, EPI><<<grid, kThreads, kSmemBytes, stream>>>(maps.a, maps.b, maps.c, maps.d, args);

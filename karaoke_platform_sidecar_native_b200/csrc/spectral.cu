@@ -561,12 +561,9 @@ cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int fr
                         const float2* twiddle, float* spec, cudaStream_t stream, int hop) {
   if (segments <= 0 || frames <= 0) return cudaSuccess;
   if (hop <= 0 || hop > kNfft) return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(stft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStftSmem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  const cudaError_t e = opt_in_smem(stft_kernel, kStftSmem, configured);
+  if (e != cudaSuccess) return e;
   stft_kernel<<<dim3((frames + kStftFramesPerCta - 1) / kStftFramesPerCta, segments), 256, kStftSmem, stream>>>(
       audio, map, frames, hop, window, twiddle, spec);
   return cudaGetLastError();
@@ -575,24 +572,18 @@ cudaError_t launch_stft(const float* audio, SegmentMap map, int segments, int fr
 cudaError_t launch_band_split(const float* spec, int segments, int frames, const float* band_wt,
                               const long long* band_wt_offset, const float* band_gamma, const int* band_gamma_offset,
                               const float* band_bias, float* x, cudaStream_t stream, int dim, int bands) {
-  static bool configured256 = false, configured512 = false;
+  static std::atomic<unsigned long long> configured256{0}, configured512{0};
   const int smem = kBandFrames * 516 * 4;   // widest band: 129 bins x 2 channels x re/im
   if (segments <= 0 || frames <= 0 || bands <= 0) return cudaSuccess;
   dim3 grid((frames + kBandFrames - 1) / kBandFrames, bands, segments);
   if (dim == 256) {
-    if (!configured256) {
-      cudaError_t e = cudaFuncSetAttribute(band_split_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-      configured256 = true;
-    }
+    const cudaError_t e = opt_in_smem(band_split_kernel<256>, smem, configured256);
+    if (e != cudaSuccess) return e;
     band_split_kernel<256><<<grid, 256, smem, stream>>>(spec, frames, band_wt, band_wt_offset, band_gamma,
                                                          band_gamma_offset, band_bias, x);
   } else if (dim == 512) {
-    if (!configured512) {
-      cudaError_t e = cudaFuncSetAttribute(band_split_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-      configured512 = true;
-    }
+    const cudaError_t e = opt_in_smem(band_split_kernel<512>, smem, configured512);
+    if (e != cudaSuccess) return e;
     band_split_kernel<512><<<grid, 512, smem, stream>>>(spec, frames, band_wt, band_wt_offset, band_gamma,
                                                          band_gamma_offset, band_bias, x);
   } else {
@@ -643,13 +634,9 @@ cudaError_t launch_row_stats(const float* x, long long rows, void* x16, float* i
 cudaError_t launch_istft_frames(const float* spec, const float* mask, int segments, int frames, const float* window,
                                 const float2* twiddle, float* frames_out, cudaStream_t stream) {
   if (segments <= 0 || frames <= 0) return cudaSuccess;
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(istft_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStftSmem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  const cudaError_t e = opt_in_smem(istft_frames_kernel, kStftSmem, configured);
+  if (e != cudaSuccess) return e;
   istft_frames_kernel<<<dim3((frames + kStftFramesPerCta - 1) / kStftFramesPerCta, segments), 256, kStftSmem,
                         stream>>>(spec, mask, frames, window, twiddle, frames_out);
   return cudaGetLastError();

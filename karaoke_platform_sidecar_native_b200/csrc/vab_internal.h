@@ -1,6 +1,7 @@
 // Internal declarations shared by the sm_100a kernels and the runtime.
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
@@ -23,6 +24,22 @@ constexpr int kNfft = 2048;
 constexpr int kHop = 512;
 constexpr int kModelFrames = 1722;
 constexpr int kBandSplitDim = 4100;  // sum of 4 * band width
+
+// A kernel's opt-in to more than 48 KB of dynamic shared memory
+// (cudaFuncSetAttribute) holds for the current device only, so it is made
+// once per device: bit d of `done` records device d.  A process that drives
+// several GPUs (one provider each) needs it on every one of them.
+template <typename K>
+inline cudaError_t opt_in_smem(K* kernel, int bytes, std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+  if (bit != 0 && (done.load(std::memory_order_relaxed) & bit) != 0) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_relaxed);
+  return e;
+}
 
 // ------------------------------------------------------------------ GEMM
 enum EpilogueKind : int {
