@@ -9,7 +9,7 @@ ties the config-3 oracle (dim 512, 62 bands, hop 441, GEGLU) to the reference.
 import numpy as np
 import pytest
 
-from karaoke_platform_sidecar_native_b200 import fixtures, modelpack as mp, stack as st
+from karaoke_platform_sidecar_native_b200 import fixtures, stack as st
 from oracle import stack_oracle as SO
 from oracle import vocalarc_oracle as O
 
