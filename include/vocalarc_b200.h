@@ -70,7 +70,8 @@ int vocalarc_b200_separate_tta(native_gpu *gpu, const float *audio, int length, 
 
 /* One clip's whole-clip forward split across `count` providers, normally one
    per GPU of one node, for the latency of a single clip (sequence parallelism;
-   no counterpart in the reference).  Each provider must have the model loaded.
+   no counterpart in the reference).  Every provider must have the same pack
+   loaded (checked by its content hash) at the same precision.
    Provider r runs the time-axis blocks for bands [90 r/count, 90 (r+1)/count)
    and the band-axis blocks for frames [T r/count, T (r+1)/count); between the
    axes the rows cross by 2-D peer copies ordered with CUDA events (x, its

@@ -213,6 +213,7 @@ struct native_gpu {
   // loaded model (vocalarc_b200_load_model)
   int model_loaded = 0;
   int model_from_cache = 0;     // the loaded weights came from a converted image on disk
+  uint64_t model_hash = 0;      // content hash of the loaded pack
   void* model_mem = nullptr;
   BlockW blocks[kDepth][2];
   BandW band;
@@ -1549,6 +1550,7 @@ int vocalarc_b200_load_model(native_gpu* g, const void* pack, size_t bytes) {
       fprintf(stderr, "vocalarc-b200: could not write the converted model to %s\n", dir.c_str());
   }
   g->tiles_frames = 0;
+  g->model_hash = want.pack_hash;
   g->model_loaded = 1;
   return 1;
 }
@@ -1668,7 +1670,8 @@ int vocalarc_b200_separate_sp(native_gpu* const* gpus, int count, const float* a
     return 0;
   }
   for (int r = 0; r < count; ++r) {
-    if (!active(gpus[r]) || !gpus[r]->model_loaded || gpus[r]->bf16 != gpus[0]->bf16 || gpus[r]->resident_active) {
+    if (!active(gpus[r]) || !gpus[r]->model_loaded || gpus[r]->bf16 != gpus[0]->bf16 || gpus[r]->resident_active ||
+        gpus[r]->model_hash != gpus[0]->model_hash) {
       fprintf(stderr, "vocalarc-b200: provider %d of the split is not ready (model, precision or open session)\n", r);
       return 0;
     }

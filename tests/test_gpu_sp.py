@@ -60,3 +60,18 @@ def test_split_rejects_too_few_frames(test_pack_blob):
         native.separate_sp(ps, np.zeros((2, 100), dtype=np.float32))   # 1 frame, 2 providers
     for p in ps:
         p.close()
+
+
+def test_split_rejects_different_models(test_pack_blob):
+    # Every provider of a split must hold the same pack (compared by content hash).
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from karaoke_platform_sidecar_native_b200 import modelpack
+    a = native.Provider(0)
+    a.load_model(test_pack_blob)
+    b = native.Provider(0)
+    b.load_model(modelpack.synthetic_pack(**modelpack.BENCH_RECIPE))
+    with pytest.raises(native.ProviderError):
+        native.separate_sp([a, b], fixtures.tone_mix(seconds=1.0, seed=9))
+    a.close()
+    b.close()
