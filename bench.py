@@ -147,15 +147,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def reference_cpu_run(pack_path, clips, threads, warmup=1):
-    """Run the reference executable over JSONL on the given clips.
+def reference_cpu_run(pack_path, clips, threads, warmup=1, exe=REF_EXE, env=None, replies=None):
+    """Run a reference executable over JSONL on the given clips.
 
-    Returns [(audio_seconds, inference_ms, wall_s)] for the clips after warmup.
+    Returns [(audio_seconds, inference_ms, wall_s)] for the clips after warmup;
+    the raw ``separated`` replies are appended to ``replies`` when given.
     """
     results = []
     with tempfile.TemporaryDirectory() as tmp:
-        proc = subprocess.Popen([REF_EXE, "--model", pack_path, "--threads", str(threads)], stdin=subprocess.PIPE,
-                                stdout=subprocess.PIPE, text=True)
+        proc = subprocess.Popen([exe, "--model", pack_path, "--threads", str(threads)], stdin=subprocess.PIPE,
+                                stdout=subprocess.PIPE, text=True, env=env)
 
         def request(obj):
             proc.stdin.write(json.dumps(obj) + "\n")
@@ -171,6 +172,8 @@ def reference_cpu_run(pack_path, clips, threads, warmup=1):
                              "vocalsPath": os.path.join(tmp, "v.wav")})
             wall = time.perf_counter() - t0
             assert reply["ok"], reply
+            if replies is not None:
+                replies.append(reply)
             if i >= warmup:
                 results.append((audio.shape[1] / 44100.0, reply["inferenceMs"], wall))
         request({"id": 99, "type": "shutdown"})
@@ -178,51 +181,139 @@ def reference_cpu_run(pack_path, clips, threads, warmup=1):
     return results
 
 
-def cpu_baseline(sample_seconds):
-    if not os.path.exists(REF_EXE):
-        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
-                "sample": "reference executable not built (make -C oracle ref)"}
-    threads = os.cpu_count() or 1
+REF_TIMER = os.path.join(ROOT, "oracle", "_ref", "ref-stage-timer")
+CFG2_CHUNKS = 27
+
+
+def reference_stage_timing(audio, reps, time_bands, band_frames, threads):
+    """The reference CPU forward's own stage functions on one clip, timed by
+    oracle/_ref/ref-stage-timer (built from native/vocalarc_separation.c in
+    place).  The front (STFT, band split) and back (final norm, mask, iSTFT) run
+    in full once; each of `reps` repetitions runs one layer pair on
+    `time_bands` bands (time axis) and `band_frames` frames (band axis).
+    Returns (frames, fixed_s, [full layer pair seconds per repetition], raw)."""
     pack = modelpack.pack_path(modelpack.BENCH_RECIPE)
-    audio = fixtures.long_mix(240.0, seed=1)
-    n = int(sample_seconds * 44100)
-    clips = [audio[:, :n // 4], audio[:, n: 2 * n]]     # short warm-up request, then the timed sample
-    res = reference_cpu_run(pack, clips, threads, warmup=1)
-    secs = sum(r[0] for r in res)
-    ms = sum(r[1] for r in res)
-    return {"value": secs / (ms / 1000.0), "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": (f"{sample_seconds:g} s excerpt of the 240 s mix through the unchanged reference CPU "
-                       f"executable (whole-clip forward, T={n // 512 + 1}); the workload's 20 s chunks "
-                       f"(T={FRAMES}) cost more per audio second (attention is O(T^2)), so this overstates "
-                       f"the CPU on the workload"),
-            "inference_ms": ms}
+    with tempfile.TemporaryDirectory() as tmp:
+        wav = os.path.join(tmp, "in.wav")
+        fixtures.write_wav_f32(wav, audio)
+        proc = subprocess.run([REF_TIMER, "--model", pack, "--wav", wav, "--threads", str(threads), "--reps", str(reps),
+                               "--time-bands", str(time_bands), "--band-frames", str(band_frames)],
+                              capture_output=True, text=True, check=True)
+    lines = [json.loads(x) for x in proc.stdout.splitlines() if x.strip()]
+    front, back, layers = lines[0], lines[-1], lines[1:-1]
+    frames = front["frames"]
+    pairs = [x["time_axis_s"] * 90.0 / x["time_bands"] + x["band_axis_s"] * frames / x["band_frames"] +
+             x["transposes_s"] for x in layers]
+    fixed = front["stft_s"] + front["band_split_s"] + back["mask_s"] + back["istft_s"]
+    return frames, fixed, pairs, {"front": front, "back": back, "layers": layers}
+
+
+def cfg2_reference_inputs():
+    """Chunk 13 of the config-2 track (881,559 samples, T = 1722) and the 10 s config-1 clip."""
+    return fixtures.demix_chunk(fixtures.long_mix(240.0, seed=1), 13), fixtures.tone_mix(10.0, seed=0)
+
+
+def cpu_baseline():
+    """The reference CPU forward on this host's cores, on the workload's own unit:
+    one T = 1722 chunk of the config-2 mix, front and back end in full, one of
+    the 16 layer pairs sampled (a third of its band sequences and frames) and
+    scaled; x 27 chunks per 240 s track (extrapolated).  The config-1 10 s
+    clip the same way for its latency."""
+    if not os.path.exists(REF_TIMER):
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
+                "sample": "reference stage timer not built (make -C oracle timer REF=...)"}
+    threads = os.cpu_count() or 1
+    chunk, clip = cfg2_reference_inputs()
+    frames, fixed, pairs, raw = reference_stage_timing(chunk, 2, 32, 576, threads)
+    chunk_s = fixed + 16 * pairs[-1]
+    c_frames, c_fixed, c_pairs, _ = reference_stage_timing(clip, 2, 32, 288, threads)
+    clip_s = c_fixed + 16 * c_pairs[-1]
+    return {"value": 240.0 / (CFG2_CHUNKS * chunk_s), "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": (f"reference CPU forward (native/vocalarc_separation.c stage functions, {threads} threads) on "
+                       f"chunk 13 of the cfg2 mix (T={frames}): STFT, band split, mask and iSTFT in full, one layer "
+                       f"pair on {raw['layers'][-1]['time_bands']} of 90 bands and "
+                       f"{raw['layers'][-1]['band_frames']} of {frames} frames scaled to the full pair, x16 layers, "
+                       f"x{CFG2_CHUNKS} chunks per 240 s track (extrapolated)"),
+            "chunk_t1722_s_extrapolated": round(chunk_s, 3), "fixed_stages_s": round(fixed, 3),
+            "layer_pair_s": round(pairs[-1], 3),
+            "clip_10s_ms_extrapolated": round(clip_s * 1000.0, 1)}
 
 
 def run_reference_arm(args, rank, world):
+    """The reference's own CPU implementation on this arm's config: each step
+    runs one sampled layer pair of a T = 1722 chunk of the cfg2 mix (a band
+    group on the time axis, six frame groups on the band axis), scaled to the
+    full pair; the chunk's STFT, band split, mask and iSTFT run in full once.
+    A step's time is the extrapolated separation of the 240 s track:
+    27 x (fixed stages + 16 x layer pair)."""
     if rank != 0:
         return 0
+    if not os.path.exists(REF_TIMER):
+        print(json.dumps({"impl": "reference", "unavailable": "reference stage timer not built"}), flush=True)
+        return 0
     threads = os.cpu_count() or 1
-    pack = modelpack.pack_path(modelpack.BENCH_RECIPE)
-    audio = fixtures.long_mix(240.0, seed=1)
-    n = int(args.reference_sample_seconds * 44100)
-    clips = [audio[:, (i % 200) * n:(i % 200 + 1) * n] for i in range(args.warmup + args.steps)]
-    res = reference_cpu_run(pack, clips, threads, warmup=args.warmup)
-    secs = sum(r[0] for r in res)
-    ms = sum(r[1] for r in res)
-    wall = sum(r[2] for r in res)
-    value = secs / (ms / 1000.0)
+    chunk, _ = cfg2_reference_inputs()
+    t0 = time.perf_counter()
+    frames, fixed, pairs, raw = reference_stage_timing(chunk, args.warmup + args.steps, 32, 192, threads)
+    wall = time.perf_counter() - t0
+    timed = pairs[args.warmup:]
+    track_s = [CFG2_CHUNKS * (fixed + 16 * p) for p in timed]
+    value = 240.0 * len(track_s) / sum(track_s)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / max(1, len(res)), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2: 240 s mix, bundled-layout model (synthetic weights)",
-                   "sample_per_step": f"{args.reference_sample_seconds:g} s excerpt, whole-clip forward"},
+        "warmup": args.warmup, "ms_per_step": 1000.0 * sum(track_s) / len(track_s), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"cfg2: 240 s stereo 44.1 kHz mix (seed 1), chunked demix, {CFG2_CHUNKS} chunks x "
+                               f"{CHUNK} samples (T={FRAMES}), bundled-layout model with synthetic N(0,0.02) weights",
+                   "sample_per_step": (f"one layer pair of chunk 13 (T={frames}) on "
+                                       f"{raw['layers'][-1]['time_bands']} of 90 bands and "
+                                       f"{raw['layers'][-1]['band_frames']} of {frames} frames, scaled; "
+                                       "x16 layers + fixed stages, x27 chunks (extrapolated)")},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": f"{args.reference_sample_seconds:g} s excerpts of the 240 s mix per step"},
-        "e2e": {"value": secs / wall, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                         "sample": "reference CPU stage functions (oracle/_ref/ref-stage-timer), see config"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "fixed_stages_s": round(fixed, 3), "run_wall_s": round(wall, 1),
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+REF_CUBLAS_EXE = os.path.join(ROOT, "oracle", "_ref", "vocalarc-separation-cublas")
+
+
+def reference_gpu_baseline(device, reps=3):
+    """The reference's optional GPU build (native_gpu_cuda.cu: cuBLAS SGEMM and
+    its own SIMT kernels, compiled unchanged for sm_100a by oracle/Makefile) on
+    this B200, with VOCALARC_GPU_TF32=1 and =0: the config-1 10 s clip
+    (whole clip, T = 862; p50 of `reps` inferenceMs and wall) and one
+    881,559-sample chunk of the config-2 mix (T = 1722).  Its host still runs
+    the STFT, band split and iSTFT on the CPU, which inferenceMs includes."""
+    if not os.path.exists(REF_CUBLAS_EXE):
+        return {"unavailable": "reference cuBLAS build not built (make -C oracle cublas)"}
+    threads = os.cpu_count() or 1
+    pack = modelpack.pack_path(modelpack.BENCH_RECIPE)
+    clip = fixtures.tone_mix(10.0, seed=0)
+    chunk = fixtures.demix_chunk(fixtures.long_mix(240.0, seed=1), 13)
+    out = {"exe": "native/vocalarc_separation.c + native/native_gpu_cuda.cu (cuBLAS), unchanged, sm_100a",
+           "device": device, "threads": threads}
+    for tf32 in ("1", "0"):
+        env = dict(os.environ, VOCALARC_GPU_TF32=tf32, CUDA_VISIBLE_DEVICES=str(device))
+        replies = []
+        res = reference_cpu_run(pack, [clip] * (reps + 1) + [chunk], threads, warmup=1, exe=REF_CUBLAS_EXE, env=env,
+                                replies=replies)
+        clip_ms = [r[1] for r in res[:reps]]
+        clip_wall = [r[2] * 1000.0 for r in res[:reps]]
+        chunk_ms = res[reps][1]
+        key = "tf32" if tf32 == "1" else "fp32"
+        out[key] = {
+            "backend": replies[-1].get("backend"),
+            "clip_10s_inference_ms_p50": round(float(np.median(clip_ms)), 1),
+            "clip_10s_wall_ms_p50": round(float(np.median(clip_wall)), 1),
+            "clip_10s_realtime_x": round(10.0 / (float(np.median(clip_ms)) / 1000.0), 2),
+            "chunk_t1722_inference_ms": round(chunk_ms, 1),
+            "cfg2_audio_s_per_s_extrapolated": round(240.0 / (27 * chunk_ms / 1000.0), 3),
+        }
+    return out
 
 
 def traffic_per_launch(kernel):
@@ -246,10 +337,13 @@ def main():
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
     parser.add_argument("--seconds", type=float, default=240.0)
-    parser.add_argument("--cpu-sample-seconds", type=float, default=2.0)
-    parser.add_argument("--reference-sample-seconds", type=float, default=1.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-latency", action="store_true", help="skip the 10 s clip latency measurement")
+    parser.add_argument("--no-batch", action="store_true", help="skip the config-5 batch (64 x 180 s tracks)")
+    parser.add_argument("--no-strong", action="store_true", help="skip one track sharded across the ranks")
+    parser.add_argument("--no-gpu-baseline", action="store_true", help="skip the reference cuBLAS build (N=1)")
+    parser.add_argument("--gpu-baseline-only", action="store_true",
+                        help="print only the reference cuBLAS build's timings on GPU 0")
     parser.add_argument("--precision", default="fp16", choices=("fp16", "bf16"))
     parser.add_argument("--ops", action="store_true",
                         help="config-4 op-level lines: time/band attention, STFT, band split")
@@ -269,6 +363,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
+    if args.gpu_baseline_only:
+        print(json.dumps({"gpu_baseline": reference_gpu_baseline(0)}), flush=True)
+        return 0
     if args.shard:
         return run_shard(args, rank, world, local_rank)
     if args.ops:
@@ -287,6 +384,8 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+    # Host-side channel of the chunk scheduler (64-byte IPC handles, barriers).
+    gloo = dist.new_group(backend="gloo") if world > 1 else None
 
     provider = native.Provider(local_rank)
     if args.precision == "bf16":
@@ -371,6 +470,12 @@ def main():
     if not np.isfinite(out_np).all():
         raise RuntimeError("non-finite vocals")
     latency = clip_latency(provider, stream) if rank == 0 and not args.no_latency else None
+    parity = bench_parity(provider, audio) if rank == 0 and args.seconds == 240.0 else None
+    batch = None if args.no_batch else cfg5_batch(provider, stream, rank, world)
+    strong = None if args.no_strong else strong_one_track(provider, stream, rank, world, gloo)
+    gpu_base = None
+    if world == 1 and not args.no_gpu_baseline:
+        gpu_base = reference_gpu_baseline(local_rank)
 
     if rank == 0:
         peaks = load_peaks()
@@ -407,7 +512,7 @@ def main():
                             "work_per_launch": work}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(args.cpu_sample_seconds)
+            cpu = cpu_baseline()
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 3), "higher_is_better": True,
@@ -422,8 +527,12 @@ def main():
                     "d2h_bytes_per_step": int(audio.nbytes), "steps": e2e_steps,
                     "api": "vocalarc_b200_separate_chunked (C-ABI, pinned host buffers)"},
             "gpu_launches": int(launches),
+            "parity": parity,
             "model_load": model_load,
             "latency_10s_clip": latency,
+            "batch_cfg5": batch,
+            "strong_one_track": strong,
+            "gpu_baseline": gpu_base,
             "roofline": roofline,
             "kernels": kernels,
             "cpu_baseline": cpu,
@@ -435,6 +544,165 @@ def main():
         dist.destroy_process_group()
     provider.close()
     return 0
+
+
+GOLDEN_CHUNK = os.path.join(ROOT, "tests", "golden", "cfg2_chunk13_bench.npz")
+
+
+def bench_parity(provider, audio):
+    """Parity of the benchmark's own forward batch at its own size: the 27
+    padded chunks of this rank's track through the whole-clip forward in one
+    device call (the chunked step without its overlap-add, same batch), chunk
+    13 against the vocals the unchanged reference CPU executable wrote for the
+    same chunk with the same pack (tests/golden/cfg2_chunk13_bench.npz)."""
+    import torch
+
+    if not os.path.exists(GOLDEN_CHUNK):
+        return {"checked": False, "why": "golden cfg2_chunk13_bench.npz missing"}
+    golden = np.load(GOLDEN_CHUNK)
+    count = fixtures.demix_chunk_count(audio.shape[1], CHUNK)
+    chunks = np.stack([fixtures.demix_chunk(audio, c, CHUNK) for c in range(count)])
+    d_in = torch.from_numpy(chunks).cuda()
+    d_out = torch.empty_like(d_in)
+    provider.separate_device(d_in, count, CHUNK, d_out)
+    provider.synchronize()
+    out = d_out[13].cpu().numpy().astype(np.float64)
+    ref = golden["vocals"].astype(np.float64)
+    err = ref - out
+    snr = 10 * np.log10((ref ** 2).sum() / max((err ** 2).sum(), 1e-300))
+    del d_in, d_out
+    return {"checked": True, "vs": "reference CPU executable, chunk 13 of the cfg2 track (T=1722), same pack",
+            "batch": count, "snr_db": round(float(snr), 2), "max_abs": float(np.abs(err).max()),
+            "bar": {"snr_db": 50.0, "max_abs": 2e-3}, "pass": bool(snr >= 50.0 and np.abs(err).max() <= 2e-3)}
+
+
+def tone_mix_device(seconds, seed, device):
+    """Config-5 recipe (the tone mix of config 1) generated on the device: f0
+    and phases drawn from numpy PCG64(seed) exactly as fixtures.tone_mix draws
+    them, the white noise from torch's CUDA generator seeded with `seed` (same
+    distribution, different samples from the CPU fixture)."""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    n = int(round(seconds * 44100))
+    f0 = rng.uniform(100.0, 800.0, size=3)
+    phase = rng.uniform(0.0, 2.0 * np.pi, size=3)
+    t = torch.arange(n, dtype=torch.float64, device=device) / 44100.0
+    tone = torch.zeros(n, dtype=torch.float64, device=device)
+    for j in range(3):
+        for k in range(1, 7):
+            tone += torch.sin(2.0 * np.pi * k * float(f0[j]) * t + k * float(phase[j])) / k
+    tone *= 0.2 / max(float(tone.abs().max()), 1e-12)
+    gen = torch.Generator(device=device).manual_seed(int(seed))
+    noise = torch.randn(2, n, generator=gen, device=device, dtype=torch.float32) * 0.05
+    return tone.float()[None, :] + noise
+
+
+def cfg5_batch(provider, stream, rank, world, tracks=64, seconds=180.0, first_seed=100):
+    """Config 5: `tracks` independent 180 s tone mixes (seeds 100..163), split
+    in contiguous blocks over the ranks; each rank separates its block in one
+    chunked device call (21 chunks per track).  One timed pass; the job time
+    is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    lo, hi = tracks * rank // world, tracks * (rank + 1) // world
+    length = int(round(seconds * 44100))
+    d_in = torch.empty(max(1, hi - lo), 2, length, device="cuda")
+    for i in range(lo, hi):
+        d_in[i - lo] = tone_mix_device(seconds, first_seed + i, d_in.device)
+    d_out = torch.empty_like(d_in)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    if hi > lo:
+        provider.separate_device(d_in, hi - lo, length, d_out, chunked=True, chunk=CHUNK, model_batch=1)
+    b.record(stream)
+    provider.synchronize()
+    torch.cuda.synchronize()
+    ms = torch.tensor([a.elapsed_time(b)], device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    finite = bool(torch.isfinite(d_out).all().item())
+    del d_in, d_out
+    return {"tracks": tracks, "seconds_per_track": seconds, "tracks_per_rank": f"{tracks // world}-{-(-tracks // world)}",
+            "chunks_per_track": chunk_count(length), "value": round(tracks * seconds / (ms / 1000.0), 2),
+            "unit": UNIT, "ms": round(ms, 1), "finite": finite,
+            "data": "seeded tone mixes generated on the device (f0/phase from numpy PCG64(seed), noise from the "
+                    "CUDA generator)"}
+
+
+def strong_one_track(provider, stream, rank, world, gloo, reps=2):
+    """One 240 s track (seed 1) with its 27 chunks sharded across the ranks:
+    contiguous ranges of >= 2 chunks, the overlap-add seam of each range
+    boundary pulled by the next rank over NVLink (CUDA IPC peer copy), every
+    rank writing its own output samples.  Per rank the phases are timed on the
+    host around the synchronous calls: forward of the range, seam exchange
+    (handle all-gather + peer copy), finish; the max over ranks is reported.
+    The limiter is chunk granularity: the busiest rank runs ceil-ish(27/N)
+    chunks of the 27, a ceiling of 27 / max chunks per rank."""
+    import torch
+    import torch.distributed as dist
+
+    from karaoke_platform_sidecar_native_b200 import native, shard
+
+    audio = fixtures.long_mix(240.0, seed=1)
+    length = audio.shape[1]
+    d_audio = torch.from_numpy(audio).cuda()
+    d_vocals = torch.zeros_like(d_audio)
+    plan = native.chunk_plan(length, CHUNK)
+    ranges = shard.chunk_ranges(plan["chunks"], world)
+    c0, c1 = ranges[rank]
+    phases = np.zeros(4)
+
+    def one():
+        if world == 1:
+            t = time.perf_counter()
+            provider.separate_device(d_audio, 1, length, d_vocals, chunked=True, chunk=CHUNK, model_batch=1)
+            provider.synchronize()
+            return np.array([time.perf_counter() - t, 0.0, 0.0, time.perf_counter() - t])
+        t0 = time.perf_counter()
+        if c1 > c0:
+            provider.range_forward(d_audio, length, c0, c1, CHUNK, 1)
+        t1 = time.perf_counter()
+        handle = provider.range_seam_export() if c1 > c0 and c1 < plan["chunks"] else None
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=gloo)
+        if c1 > c0 and c0 > 0:
+            provider.range_seam_import(handles[rank - 1])
+        provider.synchronize()
+        t2 = time.perf_counter()
+        if c1 > c0:
+            provider.range_finish(d_vocals)
+            provider.synchronize()
+        t3 = time.perf_counter()
+        dist.barrier(group=gloo)
+        return np.array([t1 - t0, t2 - t1, t3 - t2, time.perf_counter() - t0])
+
+    one()                                   # warm-up (range workspace sizes)
+    if world > 1:
+        dist.barrier()
+    for _ in range(reps):
+        phases += one()
+    phases /= reps
+    t = torch.tensor(phases, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    phases = t.cpu().numpy()
+    busiest = max(b - a for a, b in ranges)
+    del d_audio, d_vocals
+    return {"track_seconds": 240.0, "chunks": plan["chunks"], "ranges": ranges, "value": round(240.0 / phases[3], 2),
+            "unit": UNIT, "ms_per_track": round(phases[3] * 1000.0, 1),
+            "phase_ms_max_over_ranks": {"range_forward": round(phases[0] * 1000.0, 1),
+                                        "seam_exchange": round(phases[1] * 1000.0, 1),
+                                        "finish": round(phases[2] * 1000.0, 1)},
+            "granularity_ceiling_x": round(plan["chunks"] / busiest, 3), "busiest_rank_chunks": busiest,
+            "exchange": "CUDA IPC peer copy of one [3][seam] fp32 buffer per range boundary (NVLink), handles over gloo",
+            "timing": "host wall clock around the synchronous calls, mean of 2 passes, max over ranks"}
 
 
 def clip_latency(provider, stream, reps=20):

@@ -174,6 +174,14 @@ int vocalarc_b200_stage_istft(native_gpu *gpu, const float *spec, const float *m
    that can overlap on the GPU (other streams, other host threads) race. */
 int vocalarc_b200_stage_istft_noalloc(native_gpu *gpu, const float *spec, const float *mask, int segments,
                                       int length, float *audio);
+/* Check of the kernels' bounded waits (no counterpart in the reference): one
+   CTA waits, with the tcgen05 kernels' own wait loop limited to limit_us
+   microseconds (1 .. 100000), on an mbarrier for a copy that is never issued.
+   The wait runs out, the kernel records its error code and returns, and the
+   call then fails the way a kernel wait timeout fails inside a forward:
+   message on stderr, provider disabled, 0 returned.  Nothing is left in
+   flight, so the CUDA context stays usable.  -1 for a limit out of range. */
+int vocalarc_b200_stage_wait_check(native_gpu *gpu, int limit_us);
 /* Band split of spec (loaded model) -> x [segments][90][T][256] fp32. */
 int vocalarc_b200_stage_band_split(native_gpu *gpu, const float *spec, int segments, int frames, float *x);
 /* One transformer block (loaded model, layer, axis 0 = time / 1 = band) in

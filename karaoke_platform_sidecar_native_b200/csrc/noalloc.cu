@@ -17,6 +17,7 @@
 
 namespace vab {
 bool provider_view(native_gpu* g, int* device, cudaStream_t* stream, const float** window, const float2** twiddle);
+bool provider_launched(native_gpu* g, cudaError_t e, const char* what);
 }
 
 namespace {
@@ -75,13 +76,16 @@ extern "C" int vocalarc_b200_stage_istft_noalloc(native_gpu* gpu, const float* s
   if (scratch == nullptr) return 0;
   // Every frame slot that the overlap-add reads is written first by the frame
   // kernel, so nothing in the scratch has to start at zero.
-  cudaError_t e = vab::launch_istft_frames(spec, mask, segments, static_cast<int>(frames), window, twiddle, scratch,
-                                           stream);
-  if (e == cudaSuccess)
-    e = vab::launch_overlap_add(scratch, segments, static_cast<int>(frames), length, window, audio, stream);
-  if (e != cudaSuccess) {
-    fprintf(stderr, "vocalarc-b200: istft_noalloc launch failed: %s\n", cudaGetErrorString(e));
+  // The launches are checked, counted and traced like the provider's own: a
+  // launch error disables the provider (later calls return 0).
+  if (!vab::provider_launched(gpu,
+                              vab::launch_istft_frames(spec, mask, segments, static_cast<int>(frames), window, twiddle,
+                                                       scratch, stream),
+                              "istft"))
     return 0;
-  }
-  return 1;
+  return vab::provider_launched(
+             gpu, vab::launch_overlap_add(scratch, segments, static_cast<int>(frames), length, window, audio, stream),
+             "overlap-add")
+             ? 1
+             : 0;
 }

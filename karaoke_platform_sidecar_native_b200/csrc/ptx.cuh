@@ -73,24 +73,30 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t* bar, uint32_t parity
 }
 
 // Waits for the phase with the given parity to complete.  Returns false when
-// the CTA-wide abort flag is raised or the time limit passes; in the latter
-// case the first error code is recorded in *err and the abort flag is raised
-// so that the other warps of the CTA stop waiting too.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+// the CTA-wide abort flag is raised or `limit_ns` passes; in the latter case
+// the first error code is recorded in *err and the abort flag is raised so
+// that the other warps of the CTA stop waiting too.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                                int code, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 63u) == 0u) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - start > kWaitLimitNs) {
+      if (global_timer_ns() - start > limit_ns) {
         *abort_flag = 1;
         atomicCAS(err, 0, code);
         return false;
       }
     }
   }
+}
+
+// The kernels' wait: gives up after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err, int code) {
+  return mbar_wait_limit(bar, parity, abort_flag, err, code, kWaitLimitNs);
 }
 
 // ------------------------------------------------------------------ TMA

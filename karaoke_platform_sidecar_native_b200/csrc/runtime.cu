@@ -241,6 +241,10 @@ struct native_gpu {
   long long ws_tta = 0;
   float* tta_in = nullptr;
   float* tta_out = nullptr;
+  // host-injected failure (VOCALARC_B200_FAIL_AT=k): the k-th compute call of
+  // the C ABI fails as a CUDA error would (0 = off)
+  long long fail_at = 0;
+  long long abi_calls = 0;
   // launch trace: one event after every launch on the provider stream
   long long launches = 0;
   int trace = 0;
@@ -268,6 +272,19 @@ void trace_mark(native_gpu* g, const char* what) {
   cudaEvent_t ev = g->event_pool[used];
   cudaEventRecord(ev, g->stream);
   g->trace_entries.emplace_back(what, ev);
+}
+
+// Counts one compute call of the C ABI.  With VOCALARC_B200_FAIL_AT=k set
+// when the provider was created, the k-th such call fails the way a CUDA error
+// does (message on stderr, provider disabled, 0 returned), so that a caller's
+// fallback can be tested without faulting a GPU.
+bool abi_step(native_gpu* g, const char* what) {
+  ++g->abi_calls;
+  if (g->fail_at <= 0 || g->abi_calls != g->fail_at) return true;
+  fprintf(stderr, "vocalarc-b200: %s failed: injected failure (VOCALARC_B200_FAIL_AT=%lld); falling back to CPU\n",
+          what, g->fail_at);
+  g->enabled = 0;
+  return false;
 }
 
 bool launched(native_gpu* g, cudaError_t e, const char* what) {
@@ -1254,6 +1271,8 @@ bool init_context(native_gpu* g, int device) {
   snprintf(g->device_name, sizeof(g->device_name), "%s", prop.name);
   g->sm_count = prop.multiProcessorCount;
   g->debug = getenv("VOCALARC_GPU_DEBUG") != nullptr;
+  const char* fail = getenv("VOCALARC_B200_FAIL_AT");
+  g->fail_at = fail != nullptr ? atoll(fail) : 0;
   const char* prec = getenv("VOCALARC_B200_PRECISION");
   g->bf16 = prec != nullptr && strcmp(prec, "bf16") == 0;
   if (!cuda_ok(g, cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
@@ -1335,6 +1354,11 @@ bool provider_view(native_gpu* g, int* device, cudaStream_t* stream, const float
   *twiddle = g->d_twiddle;
   return true;
 }
+
+// A launch made by an entry point of another translation unit on this
+// provider's stream goes through the same bookkeeping as the provider's own:
+// an error disables the provider, the launch is counted and traced.
+bool provider_launched(native_gpu* g, cudaError_t e, const char* what) { return launched(g, e, what); }
 }  // namespace vab
 
 // ==================================================================== C ABI
@@ -1398,6 +1422,7 @@ int native_gpu_transformer(native_gpu* g, int sequences, int length, float* data
                            float* attention_output, float* gates, const native_gpu_transformer_weights* weights) {
   (void)normed; (void)qkv; (void)attention_output; (void)gates;
   if (!active(g) || sequences <= 0 || length <= 0 || weights == nullptr || g->resident_active) return 0;
+  if (!abi_step(g, "transformer")) return 0;
   cudaSetDevice(g->device);
   const long long tokens = static_cast<long long>(sequences) * length;
   if (!ensure_tokens(g, tokens)) return 0;
@@ -1415,6 +1440,7 @@ int native_gpu_transformer(native_gpu* g, int sequences, int length, float* data
 
 int native_gpu_resident_begin(native_gpu* g, int sequences, int length, const float* data) {
   if (!active(g) || sequences <= 0 || length <= 0 || g->resident_active || data == nullptr) return 0;
+  if (!abi_step(g, "resident begin")) return 0;
   cudaSetDevice(g->device);
   const long long tokens = static_cast<long long>(sequences) * length;
   if (!ensure_tokens(g, tokens)) return 0;
@@ -1435,6 +1461,7 @@ int native_gpu_resident_transformer(native_gpu* g, int sequences, int length,
   if (!active(g) || !g->resident_active || weights == nullptr ||
       static_cast<long long>(sequences) * length != g->resident_tokens)
     return 0;
+  if (!abi_step(g, "resident transformer")) return 0;
   cudaSetDevice(g->device);
   AxisPlan ax;
   if (!g->transposed && sequences == g->phys_s && length == g->phys_l) {
@@ -1451,6 +1478,7 @@ int native_gpu_resident_transformer(native_gpu* g, int sequences, int length,
 
 int native_gpu_resident_transpose(native_gpu* g, int sequences, int length) {
   if (!active(g) || !g->resident_active || static_cast<long long>(sequences) * length != g->resident_tokens) return 0;
+  if (!abi_step(g, "resident transpose")) return 0;
   const int ls = g->transposed ? g->phys_l : g->phys_s;
   const int ll = g->transposed ? g->phys_s : g->phys_l;
   if (sequences != ls || length != ll) return 0;
@@ -1460,6 +1488,7 @@ int native_gpu_resident_transpose(native_gpu* g, int sequences, int length) {
 
 int native_gpu_resident_end(native_gpu* g, float* data) {
   if (!active(g) || !g->resident_active) return 0;
+  if (!abi_step(g, "resident end")) return 0;
   cudaSetDevice(g->device);
   g->resident_active = 0;
   const float* src = g->x;
@@ -1479,6 +1508,7 @@ int native_gpu_resident_mask(native_gpu* g, int frames, const float* final_gamma
       final_gamma == nullptr || mask == nullptr)
     return 0;
   if (g->resident_tokens != static_cast<long long>(frames) * kBands) return 0;
+  if (!abi_step(g, "resident mask")) return 0;
   bool frame_major;
   if (g->phys_s == kBands && g->phys_l == frames)
     frame_major = false;
@@ -1620,7 +1650,7 @@ int vocalarc_b200_set_precision(native_gpu* g, int bf16) {
 
 int vocalarc_b200_separate_device(native_gpu* g, const float* d_audio, int tracks, int length, int chunked,
                                   int chunk_samples, int model_batch, float* d_vocals) {
-  if (!active(g)) return 0;
+  if (!active(g) || !abi_step(g, "separate")) return 0;
   cudaSetDevice(g->device);
   return separate_device_impl(g, d_audio, tracks, length, chunked, chunk_samples, model_batch, d_vocals) ? 1 : 0;
 }
@@ -1628,6 +1658,7 @@ int vocalarc_b200_separate_device(native_gpu* g, const float* d_audio, int track
 static int separate_host(native_gpu* g, const float* audio, int length, int chunked, int chunk_samples,
                          int model_batch, float* vocals) {
   if (!active(g) || audio == nullptr || vocals == nullptr || length <= 0) return 0;
+  if (!abi_step(g, "separate")) return 0;
   cudaSetDevice(g->device);
   const long long n = 2ll * length;
   if (!ensure_audio(g, n)) return 0;
@@ -1688,12 +1719,25 @@ int vocalarc_b200_separate_sp(native_gpu* const* gpus, int count, const float* a
     for (int q = 0; q < count; ++q) {
       if (gpus[q]->device == g->device) continue;
       int can = 0;
-      // Direct peer reads where the pair supports them (an already enabled pair
-      // reports an error that is cleared here, as is any refusal: the copies
-      // then go through the host).
-      if (cudaDeviceCanAccessPeer(&can, g->device, gpus[q]->device) == cudaSuccess && can)
-        cudaDeviceEnablePeerAccess(gpus[q]->device, 0);
-      cudaGetLastError();
+      // Direct peer reads where the pair supports them.  An error left by
+      // earlier work is reported, not swallowed: only the error of the enable
+      // call itself is cleared below.
+      const cudaError_t pending = cudaPeekAtLastError();
+      if (pending != cudaSuccess) {
+        cuda_ok(g, pending, "earlier CUDA call (before enabling peer access)");
+        return 0;
+      }
+      if (cudaDeviceCanAccessPeer(&can, g->device, gpus[q]->device) != cudaSuccess || !can) {
+        (void)cudaGetLastError();
+        continue;   // the copies between this pair are staged by the driver
+      }
+      const cudaError_t e = cudaDeviceEnablePeerAccess(gpus[q]->device, 0);
+      if (e != cudaSuccess) {
+        (void)cudaGetLastError();   // exactly the error of the enable call
+        if (e != cudaErrorPeerAccessAlreadyEnabled)
+          fprintf(stderr, "vocalarc-b200: peer access %d -> %d refused (%s); copies are staged by the driver\n",
+                  g->device, gpus[q]->device, cudaGetErrorString(e));
+      }
     }
   }
   cudaSetDevice(g0->device);
@@ -1920,6 +1964,7 @@ int vocalarc_b200_range_finish(native_gpu* g, float* d_vocals) {
 int vocalarc_b200_separate_tta(native_gpu* g, const float* audio, int length, int chunk_samples, int model_batch,
                                int bigshifts, int tta, float* vocals) {
   if (!active(g) || audio == nullptr || vocals == nullptr || length <= 0) return 0;
+  if (!abi_step(g, "separate")) return 0;
   cudaSetDevice(g->device);
   const int shifts = bigshifts < 1 ? 1 : bigshifts;
   const int variants = tta ? 3 : 1;
@@ -1954,6 +1999,16 @@ int vocalarc_b200_synchronize(native_gpu* g) {
 }
 
 void* vocalarc_b200_stream(native_gpu* g) { return g == nullptr ? nullptr : static_cast<void*>(g->stream); }
+
+int vocalarc_b200_stage_wait_check(native_gpu* g, int limit_us) {
+  if (limit_us < 1 || limit_us > 100000) return -1;
+  if (!active(g)) return 0;
+  cudaSetDevice(g->device);
+  if (!launched(g, launch_wait_check(g->d_err, static_cast<unsigned long long>(limit_us) * 1000ull, g->stream),
+                "wait check"))
+    return 0;
+  return sync_and_check(g, "wait check") ? 1 : 0;
+}
 
 int vocalarc_b200_take_device_error(native_gpu* g) {
   if (g == nullptr || g->d_err == nullptr) return -1;

@@ -196,6 +196,9 @@ cudaError_t launch_demix_range(const float* seg_out, SegmentMap map, int chunks,
 cudaError_t launch_tta_inputs(const float* mix, int n, int shifts, int variants, float* out, cudaStream_t stream);
 cudaError_t launch_tta_combine(const float* est, int n, int shifts, int tta, float* vocals, cudaStream_t stream);
 cudaError_t launch_transpose_tokens(const float* src, float* dst, int s0, int l0, cudaStream_t stream);
+// One CTA waiting, with the kernels' wait loop and the given limit, on an
+// mbarrier that never completes; records kErrWaitTma in *err and returns.
+cudaError_t launch_wait_check(int* err, unsigned long long limit_ns, cudaStream_t stream);
 cudaError_t upload_band_tables(const int* first, const int* dims);
 
 }  // namespace vab

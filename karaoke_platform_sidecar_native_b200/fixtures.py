@@ -77,6 +77,54 @@ def long_mix(seconds: float, seed: int = 1) -> np.ndarray:
     return out.astype(np.float32)
 
 
+CHUNK_SAMPLES = 881_559          # the ONNX sidecar's chunk (onnx/native/onnx_sidecar.cpp:53)
+
+
+def demix_chunk_count(length: int, chunk: int = CHUNK_SAMPLES) -> int:
+    """Number of chunks the chunked demix cuts a ``length``-sample track into."""
+    step = chunk // 2
+    border = chunk - step
+    padded = length + 2 * border if length > 2 * border else length
+    return -(-padded // step)
+
+
+def demix_chunk(mix: np.ndarray, index: int, chunk: int = CHUNK_SAMPLES) -> np.ndarray:
+    """Input of chunk ``index`` of the chunked demix, as the device path forms it.
+
+    The track is reflect-padded by ``border = chunk - chunk//2`` samples on both
+    sides (``Separator::demix`` onnx_sidecar.cpp:725-737), chunk ``index``
+    starts at ``index * (chunk//2)`` of the padded track and a short final chunk
+    is reflect-filled when more than half of it is real (``pad_chunk`` :366-383)
+    or zero-filled otherwise.  Used to feed single chunks to the whole-clip
+    forward, e.g. to check one chunk of a chunked run at its full size.
+    """
+    mix = np.asarray(mix, dtype=np.float32)
+    length = mix.shape[1]
+    step = chunk // 2
+    border = chunk - step
+
+    def reflect(i, n):
+        if n <= 1:
+            return np.zeros_like(i)
+        period = 2 * n - 2
+        r = np.mod(i, period)
+        return np.where(r >= n, period - r, r)
+
+    padded = length + 2 * border if length > 2 * border else length
+    start = index * step
+    if start >= padded:
+        raise ValueError(f"chunk {index} starts past the padded track ({padded} samples)")
+    available = min(padded - start, chunk)
+    pos = np.arange(start, start + available)
+    src = reflect(pos - border, length) if padded != length else pos
+    out = np.zeros((mix.shape[0], chunk), dtype=np.float32)
+    out[:, :available] = mix[:, src]
+    if chunk // 2 < available < chunk and available > 1:
+        fill = reflect(np.arange(available, chunk), available)
+        out[:, available:] = out[:, fill]
+    return out
+
+
 def batch_mixes(count: int = 64, seconds: float = 180.0, first_seed: int = 100) -> list:
     """Config-5 recipe: ``count`` tone mixes with seeds first_seed.. (lazy list)."""
     return [(first_seed + i, seconds) for i in range(count)]

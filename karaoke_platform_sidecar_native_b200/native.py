@@ -99,6 +99,7 @@ _SIGNATURES = {
     "vocalarc_b200_stage_stft": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     "vocalarc_b200_stage_istft": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     "vocalarc_b200_stage_istft_noalloc": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "vocalarc_b200_stage_wait_check": (ctypes.c_int, [_vp, ctypes.c_int]),
     "vocalarc_b200_stage_band_split": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     "vocalarc_b200_stage_block": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "vocalarc_b200_stage_mask": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
@@ -354,6 +355,10 @@ class Provider:
     def stage_istft_noalloc(self, spec, mask, segments, length, audio):
         self.check(self.lib.vocalarc_b200_stage_istft_noalloc(self.handle, dptr(spec), dptr(mask), segments, length,
                                                               dptr(audio)), "stage_istft_noalloc")
+
+    def stage_wait_check(self, limit_us: int) -> int:
+        """Run the bounded-wait check; returns the raw C-ABI result (0 = the wait ran out and was reported)."""
+        return int(self.lib.vocalarc_b200_stage_wait_check(self.handle, limit_us))
 
     def stage_band_split(self, spec, segments, frames, x):
         self.check(self.lib.vocalarc_b200_stage_band_split(self.handle, dptr(spec), segments, frames, dptr(x)),

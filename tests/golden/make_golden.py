@@ -2,7 +2,8 @@
 
 Run where the reference sources are checked out (``make -C oracle ref REF=<reference>/native``):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py            # the small cases (seconds)
+    python tests/golden/make_golden.py --large    # the benchmarked sizes (about 20 min on 8 cores)
 
 For each case it writes a seeded float32 WAV, runs ``oracle/_ref/vocalarc-separation``
 (built from native/vocalarc_separation.c by oracle/Makefile) over the JSONL
@@ -40,6 +41,28 @@ CASES = {
 }
 BANDS_KEPT = (0, 24, 60, 88, 89)
 
+#: The sizes the benchmark runs, with both synthetic packs (parity recipe and
+#: benchmark recipe).  case -> (input, pack recipe, frames kept)
+#:   cfg1_10s_*    config 1: the 10 s seed-0 tone mix, whole clip, T = 862
+#:   cfg2_chunk13_*  config 2: chunk 13 of the 27 chunks of the 240 s seed-1
+#:                   mix (reflect border pad, pad_chunk), 881,559 samples,
+#:                   T = 1722 -- one unit of the chunked benchmark
+#: The input audio is not stored (it is regenerated from the seed); its sha256
+#: is, so a test can confirm it rebuilt the same samples.
+LARGE_CASES = {
+    "cfg1_10s_test": (("tone", 10.0, 0), "TEST", (0, 1, 430, 860, 861)),
+    "cfg1_10s_bench": (("tone", 10.0, 0), "BENCH", (0, 1, 430, 860, 861)),
+    "cfg2_chunk13_test": (("chunk", 240.0, 1, 13), "TEST", (0, 1, 861, 1720, 1721)),
+    "cfg2_chunk13_bench": (("chunk", 240.0, 1, 13), "BENCH", (0, 1, 861, 1720, 1721)),
+}
+
+
+def large_input(spec) -> np.ndarray:
+    if spec[0] == "tone":
+        return fixtures.tone_mix(spec[1], spec[2])
+    mix = fixtures.long_mix(spec[1], spec[2])
+    return fixtures.demix_chunk(mix, spec[3])
+
 
 def run_reference(pack: str, wav: str, vocals: str, dump: str, threads: int = 8) -> dict:
     requests = [
@@ -54,6 +77,38 @@ def run_reference(pack: str, wav: str, vocals: str, dump: str, threads: int = 8)
     lines = [json.loads(x) for x in proc.stdout.splitlines() if x.strip()]
     assert lines[1]["ok"], proc.stdout
     return lines[1]
+
+
+def main_large(names) -> None:
+    for name in names:
+        spec, recipe, frames_kept = LARGE_CASES[name]
+        pack = modelpack.pack_path(modelpack.TEST_RECIPE if recipe == "TEST" else modelpack.BENCH_RECIPE)
+        digest = hashlib.sha256(open(pack, "rb").read()).hexdigest()
+        audio = large_input(spec)
+        with tempfile.TemporaryDirectory() as tmp:
+            wav = os.path.join(tmp, "in.wav")
+            fixtures.write_wav_f32(wav, audio)
+            vocals_path = os.path.join(tmp, "vocals.wav")
+            prefix = os.path.join(tmp, "d")
+            reply = run_reference(pack, wav, vocals_path, prefix)
+            frames = reply["frames"]
+
+            def dump(stage, shape):
+                return np.fromfile(f"{prefix}-{stage}.f32", dtype=np.float32).reshape(shape)
+
+            fk = list(frames_kept)
+            mask = dump("mask", (1025, 2, frames, 2))[:, :, fk, :]
+            f16 = dump("features16", (frames, 90, 256))[fk]
+            vocals = fixtures.read_wav_f32(vocals_path)
+            np.savez_compressed(
+                os.path.join(HERE, f"{name}.npz"),
+                vocals=vocals, mask=np.ascontiguousarray(mask), features16=f16,
+                frames_kept=np.array(frames_kept), frames=np.array(frames),
+                audio_sha256=np.array(hashlib.sha256(np.ascontiguousarray(audio).tobytes()).hexdigest()),
+                pack_sha256=np.array(digest), recipe=np.array(recipe),
+                inference_ms=np.array(float(reply.get("inferenceMs", -1))))
+            print(name, "frames", frames, "inferenceMs", reply.get("inferenceMs"),
+                  "vocals rms", float(np.sqrt((vocals ** 2).mean())), flush=True)
 
 
 def main() -> None:
@@ -90,4 +145,8 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    if "--large" in sys.argv:
+        chosen = [a for a in sys.argv[1:] if a in LARGE_CASES]
+        main_large(chosen or list(LARGE_CASES))
+    else:
+        main()

@@ -88,6 +88,7 @@ def attention_reference(qkv, gates, d1, d2, d3, pos_dim):
 
 @pytest.mark.parametrize("d1,d2,d3,pos_dim", [
     (1, 3, 1, 1), (2, 5, 2, 1), (87, 4, 1, 1), (128, 2, 1, 1), (129, 3, 1, 1), (300, 2, 2, 1), (862, 2, 1, 1),
+    (1722, 3, 1, 1), (1723, 2, 1, 1),     # the benchmark's chunk length (14 key tiles, 58-row tail) and one more
     (7, 90, 1, 2), (26, 90, 2, 2), (3, 62, 1, 2), (5, 1, 1, 2), (9, 2, 1, 2)])
 def test_attention_matches_fp32_softmax(provider, d1, d2, d3, pos_dim):
     rows = d1 * d2 * d3

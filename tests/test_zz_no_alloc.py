@@ -56,7 +56,11 @@ def test_noalloc_istft_matches_regular_entry_point_twice():
             snr = 10 * np.log10((a ** 2).sum() / max(((a - b) ** 2).sum(), 1e-300))
             assert snr > 100
         # A request beyond the fixed scratch (2048 frames) is refused, not run.
-        spec, mask = _inputs(3, 1, 1000)
+        # The buffers have the requested size (3 x 1722 frames, about 85 MB
+        # each), so even a broken size check could not read past them.
+        frames = 881559 // 512 + 1
+        spec = torch.zeros(3, frames, 1025, 2, 2, device="cuda")
+        mask = torch.zeros_like(spec)
         out = torch.zeros(3, 2, 881559, device="cuda")
         ok = provider.lib.vocalarc_b200_stage_istft_noalloc(provider.handle, native.dptr(spec), native.dptr(mask), 3,
                                                             881559, native.dptr(out))
