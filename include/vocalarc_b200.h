@@ -86,6 +86,27 @@ int vocalarc_b200_separate_tta(native_gpu *gpu, const float *audio, int length, 
 int vocalarc_b200_separate_sp(native_gpu *const *gpus, int count, const float *audio, int length, float *vocals);
 int vocalarc_b200_sp_plan(int count, int frames, int phase, long long *out, int capacity);
 
+/* Batch separation of WAV files with the file I/O off the critical path: a
+   reader thread decodes track i+1 and a writer thread writes track i-1 while
+   the device separates track i (whole-clip forward, or chunked when chunked
+   != 0).  Inputs are read like the reference host reads them (wav_read,
+   to_stereo, resample_linear: PCM 16/24/32-bit or float32, mono or stereo,
+   any rate, resampled linearly to 44.1 kHz; vocalarc_separation.c:1152-1222);
+   outputs are float32 stereo 44.1 kHz WAVs with non-finite samples written as
+   0 (wav_write :1224-1237): vocals_paths[i] and, when instrumental_paths and
+   its entry are non-NULL and non-empty, instrumental = mix - vocals
+   (:1587-1593).  Returns the number of tracks whose outputs were written;
+   failures are reported on stderr. */
+int vocalarc_b200_separate_files(native_gpu *gpu, int count, const char *const *input_paths,
+                                 const char *const *vocals_paths, const char *const *instrumental_paths,
+                                 int chunked);
+/* The reader stage alone (host only, no GPU): the decoded planar stereo
+   44.1 kHz track of `path` into out[2][*length]; out NULL only sets *length;
+   0 when unreadable or capacity < 2 * length floats.  write_track is the
+   writer stage: float32 stereo 44.1 kHz, non-finite samples as 0. */
+int vocalarc_b200_read_track(const char *path, float *out, long long capacity, int *length);
+int vocalarc_b200_write_track(const char *path, const float *audio, int length);
+
 /* Device-pointer variants on the provider's stream; they return after
    enqueueing (call vocalarc_b200_synchronize).  `tracks` planar clips of
    `length` samples each are laid out back to back ([tracks][2][length]). */

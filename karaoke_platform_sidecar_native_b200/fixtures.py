@@ -142,6 +142,38 @@ def write_wav_f32(path: str, audio: np.ndarray, rate: int = RATE) -> None:
         handle.write(header + data)
 
 
+def wav_bytes(audio: np.ndarray, rate: int = RATE, bits: int = 32, pcm: bool = False,
+              extra_chunk: bytes = b"") -> bytes:
+    """WAV file bytes of planar ``[channels][n]`` audio: float32 (format 3) or
+    PCM 16/24/32-bit (format 1, values clipped to [-1, 1) and rounded).
+    ``extra_chunk`` is inserted before "fmt " (e.g. a LIST chunk) to exercise
+    chunk walking; odd-sized chunks get their pad byte."""
+    audio = np.asarray(audio, dtype=np.float32)
+    channels, n = audio.shape
+    frames = np.ascontiguousarray(audio.T)
+    if not pcm:
+        data = frames.astype("<f4").tobytes()
+        fmt_code, bits = 3, 32
+    else:
+        fmt_code = 1
+        scale = float(2 ** (bits - 1))
+        ints = np.clip(np.round(frames.astype(np.float64) * scale), -scale, scale - 1).astype(np.int64)
+        if bits == 16:
+            data = ints.astype("<i2").tobytes()
+        elif bits == 32:
+            data = ints.astype("<i4").tobytes()
+        else:
+            u = (ints & 0xFFFFFF).astype(np.uint32)
+            b = np.stack([u & 0xFF, (u >> 8) & 0xFF, (u >> 16) & 0xFF], axis=-1).astype(np.uint8)
+            data = b.tobytes()
+    width = bits // 8
+    fmt = struct.pack("<HHIIHH", fmt_code, channels, rate, rate * channels * width, channels * width, bits)
+    body = b"WAVE" + extra_chunk + b"fmt " + struct.pack("<I", 16) + fmt + b"data" + struct.pack("<I", len(data)) + data
+    if len(data) & 1:
+        body += b"\0"
+    return b"RIFF" + struct.pack("<I", len(body)) + body
+
+
 def read_wav_f32(path: str) -> np.ndarray:
     """Read a float32 (format 3) WAV into planar ``[channels][n]``."""
     raw = open(path, "rb").read()

@@ -100,6 +100,12 @@ _SIGNATURES = {
     "vocalarc_b200_stage_istft": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     "vocalarc_b200_stage_istft_noalloc": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     "vocalarc_b200_stage_wait_check": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "vocalarc_b200_separate_files": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                                    ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p),
+                                                    ctypes.c_int]),
+    "vocalarc_b200_read_track": (ctypes.c_int, [ctypes.c_char_p, _f32p, ctypes.c_longlong,
+                                                ctypes.POINTER(ctypes.c_int)]),
+    "vocalarc_b200_write_track": (ctypes.c_int, [ctypes.c_char_p, _f32p, ctypes.c_int]),
     "vocalarc_b200_stage_band_split": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     "vocalarc_b200_stage_block": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "vocalarc_b200_stage_mask": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
@@ -115,6 +121,25 @@ def chunk_plan(length: int, chunk: int = 0) -> dict:
     if not lib.vocalarc_b200_chunk_plan(length, chunk, *[ctypes.byref(v) for v in vals]):
         raise ProviderError(f"chunk_plan({length}, {chunk}) failed")
     return dict(zip(("chunks", "step", "border", "seam"), (v.value for v in vals)))
+
+
+def read_track(path: str) -> np.ndarray:
+    """The batch reader stage: a WAV decoded to planar stereo float32 at 44.1 kHz (no GPU)."""
+    lib = load()
+    n = ctypes.c_int(0)
+    if not lib.vocalarc_b200_read_track(os.fsencode(path), None, 0, ctypes.byref(n)):
+        raise ProviderError(f"cannot read {path}")
+    out = np.zeros((2, n.value), dtype=np.float32)
+    if not lib.vocalarc_b200_read_track(os.fsencode(path), fptr(out), out.size, ctypes.byref(n)):
+        raise ProviderError(f"cannot read {path}")
+    return out
+
+
+def write_track(path: str, audio: np.ndarray) -> None:
+    """The batch writer stage: float32 stereo 44.1 kHz WAV, non-finite samples as 0 (no GPU)."""
+    audio = np.ascontiguousarray(audio, dtype=np.float32)
+    if not load().vocalarc_b200_write_track(os.fsencode(path), fptr(audio), audio.shape[1]):
+        raise ProviderError(f"cannot write {path}")
 
 
 def sp_plan(count: int, frames: int, phase: int) -> np.ndarray:
@@ -355,6 +380,14 @@ class Provider:
     def stage_istft_noalloc(self, spec, mask, segments, length, audio):
         self.check(self.lib.vocalarc_b200_stage_istft_noalloc(self.handle, dptr(spec), dptr(mask), segments, length,
                                                               dptr(audio)), "stage_istft_noalloc")
+
+    def separate_files(self, inputs, vocals, instrumentals=None, chunked: bool = False) -> int:
+        """Separate WAV files with the reader and writer stages running beside the device work."""
+        n = len(inputs)
+        arr = lambda paths: (ctypes.c_char_p * n)(*[os.fsencode(p) if p else None for p in paths])
+        return int(self.lib.vocalarc_b200_separate_files(self.handle, n, arr(inputs), arr(vocals),
+                                                         arr(instrumentals) if instrumentals else None,
+                                                         1 if chunked else 0))
 
     def stage_wait_check(self, limit_us: int) -> int:
         """Run the bounded-wait check; returns the raw C-ABI result (0 = the wait ran out and was reported)."""

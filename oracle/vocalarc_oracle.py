@@ -408,3 +408,78 @@ def separate_tta(separate, mix: np.ndarray, bigshifts: int = 2, tta: bool = True
     total = (vocals + F32(1.0) * restored).astype(F32)
     total = (total + F32(-1.0) * inverted).astype(F32)
     return (total * F32(1.0 / 3.0)).astype(F32)
+
+
+# --------------------------------------------------------------- host WAV input
+def wav_decode(raw: bytes):
+    """``wav_read`` (vocalarc_separation.c:1152-1187): (planar float32 [channels][n], rate).
+
+    RIFF/WAVE chunks are walked in order (the last "fmt " of >= 16 bytes and
+    the last "data" win; a chunk running past the end stops the walk); PCM
+    16/24/32-bit (format 1) or float32 (format 3), 1 or 2 channels.
+    """
+    if len(raw) < 44 or raw[:4] != b"RIFF" or raw[8:12] != b"WAVE":
+        raise ValueError("unsupported WAV input")
+    fmt = None
+    data = None
+    offset = 12
+    while offset + 8 <= len(raw):
+        size = int.from_bytes(raw[offset + 4:offset + 8], "little")
+        payload = offset + 8
+        if payload > len(raw) or size > len(raw) - payload:
+            break
+        tag = raw[offset:offset + 4]
+        if tag == b"fmt " and size >= 16:
+            body = raw[payload:payload + 16]
+            fmt = (int.from_bytes(body[0:2], "little"), int.from_bytes(body[2:4], "little"),
+                   int.from_bytes(body[4:8], "little"), int.from_bytes(body[14:16], "little"))
+        elif tag == b"data":
+            data = raw[payload:payload + size]
+        offset = payload + size + (size & 1)
+    if fmt is None or data is None:
+        raise ValueError("WAV without fmt or data")
+    form, channels, rate, bits = fmt
+    if not (1 <= channels <= 2 and rate >= 1 and (form == 3 and bits == 32 or form == 1 and bits in (16, 24, 32))):
+        raise ValueError("WAV must be PCM16/24/32 or float32 mono/stereo")
+    width = bits // 8
+    n = len(data) // (channels * width)
+    body = np.frombuffer(data[:n * channels * width], dtype=np.uint8).reshape(n, channels, width)
+    if form == 3:
+        values = body.copy().view("<f4")[..., 0]
+    elif bits == 16:
+        values = body.copy().view("<i2")[..., 0].astype(F32) / F32(32768.0)
+    elif bits == 24:
+        v = body[..., 0].astype(np.int32) | (body[..., 1].astype(np.int32) << 8) | (body[..., 2].astype(np.int32) << 16)
+        v = np.where(v & 0x800000, v | ~0xFFFFFF, v).astype(np.int32)
+        values = v.astype(F32) / F32(8388608.0)
+    else:
+        values = body.copy().view("<i4")[..., 0].astype(F32) / F32(2147483648.0)
+    return np.ascontiguousarray(values.T.astype(F32)), rate
+
+
+def to_stereo(planar: np.ndarray) -> np.ndarray:
+    """``to_stereo`` (vocalarc_separation.c:1189-1196): mono is duplicated."""
+    return planar if planar.shape[0] == 2 else np.concatenate([planar, planar], axis=0)
+
+
+def resample_linear(audio: np.ndarray, input_rate: int, output_rate: int = 44100) -> np.ndarray:
+    """``resample_linear`` (vocalarc_separation.c:1198-1222): align_corners=False
+    linear interpolation, output length llround(n * out / in) (at least 1)."""
+    n = audio.shape[1]
+    length = max(1, int(np.floor(n * output_rate / input_rate + 0.5)))
+    i = np.arange(length, dtype=np.float64)
+    position = np.maximum((i + 0.5) * input_rate / output_rate - 0.5, 0.0)
+    upper = np.minimum(position + 1.0, n - 1)
+    lower_i = position.astype(np.int64)
+    upper_i = upper.astype(np.int64)
+    fraction = (position - lower_i).astype(F32)
+    one = F32(1.0)
+    return (audio[:, lower_i] * (one - fraction) + audio[:, upper_i] * fraction).astype(F32)
+
+
+def read_track(raw: bytes) -> np.ndarray:
+    """A host request's input as ``separate`` prepares it (:1568-1572): decoded,
+    stereo, resampled to 44.1 kHz when needed."""
+    planar, rate = wav_decode(raw)
+    stereo = to_stereo(planar)
+    return stereo if rate == 44100 else resample_linear(stereo, rate)

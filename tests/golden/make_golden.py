@@ -4,6 +4,7 @@ Run where the reference sources are checked out (``make -C oracle ref REF=<refer
 
     python tests/golden/make_golden.py            # the small cases (seconds)
     python tests/golden/make_golden.py --large    # the benchmarked sizes (about 20 min on 8 cores)
+    python tests/golden/make_golden.py --wav      # host input conversion (PCM16 mono 22.05 kHz)
 
 For each case it writes a seeded float32 WAV, runs ``oracle/_ref/vocalarc-separation``
 (built from native/vocalarc_separation.c by oracle/Makefile) over the JSONL
@@ -111,6 +112,31 @@ def main_large(names) -> None:
                   "vocals rms", float(np.sqrt((vocals ** 2).mean())), flush=True)
 
 
+#: Host input conversion (wav_read, to_stereo, resample_linear): a PCM16 mono
+#: 22.05 kHz WAV through the reference executable; its "source" dump is the
+#: STFT of the converted 44.1 kHz stereo input.
+WAV_CASE = "wav_pcm16_mono_22k"
+
+
+def main_wav() -> None:
+    pack = modelpack.pack_path(modelpack.TEST_RECIPE)
+    digest = hashlib.sha256(open(pack, "rb").read()).hexdigest()
+    mono = fixtures.tone_mix(0.25, 21)[:1, ::2]                     # 5513 samples at 22.05 kHz
+    raw = fixtures.wav_bytes(mono, rate=22050, bits=16, pcm=True, extra_chunk=b"LIST" + (3).to_bytes(4, "little") + b"abc\0")
+    with tempfile.TemporaryDirectory() as tmp:
+        wav = os.path.join(tmp, "in.wav")
+        open(wav, "wb").write(raw)
+        vocals_path = os.path.join(tmp, "vocals.wav")
+        prefix = os.path.join(tmp, "d")
+        reply = run_reference(pack, wav, vocals_path, prefix)
+        frames = reply["frames"]
+        source = np.fromfile(f"{prefix}-source.f32", dtype=np.float32).reshape(1025, 2, frames, 2)
+        vocals = fixtures.read_wav_f32(vocals_path)
+        np.savez_compressed(os.path.join(HERE, f"{WAV_CASE}.npz"), wav=np.frombuffer(raw, dtype=np.uint8),
+                            source=source, vocals=vocals, frames=np.array(frames), pack_sha256=np.array(digest))
+        print(WAV_CASE, "frames", frames, "length", vocals.shape[1])
+
+
 def main() -> None:
     pack = modelpack.pack_path(modelpack.TEST_RECIPE)
     digest = hashlib.sha256(open(pack, "rb").read()).hexdigest()
@@ -145,7 +171,9 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    if "--large" in sys.argv:
+    if "--wav" in sys.argv:
+        main_wav()
+    elif "--large" in sys.argv:
         chosen = [a for a in sys.argv[1:] if a in LARGE_CASES]
         main_large(chosen or list(LARGE_CASES))
     else:

@@ -1,6 +1,6 @@
-"""The reference's own C host over this provider: fallback, non-resident path, full-device hook.
+"""The reference's own C host over this provider (fallback, non-resident path, full-device hook) and the WAV batch pipeline.
 
-All three executables are the unchanged reference JSONL host
+Both executables are the unchanged reference JSONL host
 (native/vocalarc_separation.c) built by oracle/Makefile:
   * ``vocalarc-separation-b200``       linked to this provider (drop-in);
   * ``vocalarc-separation-b200-hook``  the same plus the guarded hook of
@@ -142,3 +142,40 @@ def test_bounded_wait_runs_out_and_is_reported(capfd, test_pack_blob):
         assert snr_db(g["vocals"], vocals) >= SNR_BAR_DB
     finally:
         q.close()
+
+
+# ------------------------------------------------------------------ batch with WAV I/O off the critical path
+def test_separate_files_pipeline(tmp_path, test_pack_blob):
+    # Three inputs in three formats through the reader / device / writer
+    # pipeline: every vocals file equals the provider's own separation of the
+    # decoded input bit for bit, instrumental = mix - vocals, and the PCM16
+    # mono 22.05 kHz input matches the reference executable's vocals.
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    g = np.load(os.path.join(GOLDEN, "wav_pcm16_mono_22k.npz"))
+    rng = np.random.default_rng(5)
+    inputs = [tmp_path / "a.wav", tmp_path / "b.wav", tmp_path / "c.wav"]
+    inputs[0].write_bytes(g["wav"].tobytes())
+    inputs[1].write_bytes(fixtures.wav_bytes(fixtures.tone_mix(0.7, 3)))
+    inputs[2].write_bytes(fixtures.wav_bytes((rng.standard_normal((2, 30000)) * 0.1).astype(np.float32),
+                                             rate=48000, bits=24, pcm=True))
+    vocals = [tmp_path / f"v{i}.wav" for i in range(3)]
+    inst = [tmp_path / f"i{i}.wav" for i in range(3)]
+    p = native.Provider(0)
+    try:
+        p.load_model(test_pack_blob)
+        assert p.separate_files([str(x) for x in inputs], [str(x) for x in vocals], [str(x) for x in inst]) == 3
+        for i in range(3):
+            mix = native.read_track(str(inputs[i]))
+            v = fixtures.read_wav_f32(str(vocals[i]))
+            assert np.array_equal(v, p.separate(mix))
+            assert np.array_equal(fixtures.read_wav_f32(str(inst[i])), (mix - v).astype(np.float32))
+        assert snr_db(g["vocals"], fixtures.read_wav_f32(str(vocals[0]))) >= SNR_BAR_DB
+        # An unreadable input is skipped and reported; the others are written.
+        (tmp_path / "bad.wav").write_bytes(b"not a wav")
+        assert p.separate_files([str(tmp_path / "bad.wav"), str(inputs[1])],
+                                [str(tmp_path / "vb.wav"), str(tmp_path / "v1b.wav")]) == 1
+        assert np.array_equal(fixtures.read_wav_f32(str(tmp_path / "v1b.wav")),
+                              fixtures.read_wav_f32(str(vocals[1])))
+    finally:
+        p.close()
