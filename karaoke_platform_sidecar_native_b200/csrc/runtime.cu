@@ -399,10 +399,6 @@ bool make_out16_map(native_gpu* g, CUtensorMap* map, const void* base, long long
   return make_tmap_2d(map, base, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(rows),
                       static_cast<uint64_t>(n) * 2, 64, 32, 128, g->bf16 != 0);
 }
-bool make_resid_maps(native_gpu* g, GemmMaps& maps, long long rows) {
-  return make_tmap_2d(&maps.c, g->x, 4, kDim, static_cast<uint64_t>(rows), kDim * 4ull, 32, 32, 128, false) &&
-         make_tmap_2d(&maps.d, g->x16, 2, kDim, static_cast<uint64_t>(rows), kDim * 2ull, 32, 32, 64, g->bf16 != 0);
-}
 
 // Scales column i of W[out][in] by scale[i] (an RMSNorm gamma folded into the
 // GEMM that consumes the norm).
@@ -586,11 +582,6 @@ GemmArgs uniform_args(native_gpu* g, long long rows, int n, int k) {
 }
 
 // ------------------------------------------------------------------ one axial block
-// Token grid (d1, d2, d3): row = (i3 * d2 + i2) * d1 + i1.  Positions run along
-// dim `pos_dim`; the RoPE position of row r is (r / pos_div) % pos_mod.
-struct AxisPlan {
-  int pos_dim, d1, d2, d3, sequences, length, pos_div, pos_mod;
-};
 
 bool ensure_stats(native_gpu* g, long long tokens, int remap_s0 = 0, int remap_l0 = 0) {
   if (g->stats_valid && remap_s0 == 0) return true;
@@ -601,74 +592,21 @@ bool ensure_stats(native_gpu* g, long long tokens, int remap_s0 = 0, int remap_l
   return true;
 }
 
+bool provider_hook(void* owner, cudaError_t e, const char* what) {
+  return launched(static_cast<native_gpu*>(owner), e, what);
+}
+
 // One axial block on the residual stream g->x (transformer_forward,
-// vocalarc_separation.c:836-873).  Needs x16 / row_inv of the current x; leaves
-// them valid for the updated x.
+// vocalarc_separation.c:836-873) through the shared orchestration of
+// block.cu.  Needs x16 / row_inv of the current x; leaves them valid for the
+// updated x.
 bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan& ax) {
-  const bool bf = g->bf16 != 0;
   if (!ensure_rope(g, ax.length) || !ensure_stats(g, tokens)) return false;
-  GemmMaps maps;
-  // q|k|v = RoPE(inv * x16 (gamma o Wqkv)^T), gates = sigmoid(inv * x16 (gamma o Wg)^T + b)
-  if (!make_map_rows(g, &maps.a, g->x16, tokens, kDim, 128) || !make_out16_map(g, &maps.c, g->qkv, tokens, kQkvDim))
+  const AxialBuffers buf{g->x, g->x16, g->row_inv, nullptr, g->qkv, g->attn, g->gates, g->d_rope, g->d_err};
+  const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.gate_b, w.ff1_b, w.ff2_b};
+  if (!run_axial_block(buf, aw, AxialShape{kDim, kFfDim, 0}, tokens, ax, g->bf16 != 0, g->sm_count, g->stream,
+                       provider_hook, g))
     return false;
-  maps.b = w.m_qkv;
-  maps.d = maps.c;
-  GemmArgs args = uniform_args(g, tokens, kQkvDim, kDim);
-  args.gate_tile = 1;
-  args.num_tiles = static_cast<int>((tokens + 127) / 128) * (args.n_tiles + 1);
-  args.row_inv = g->row_inv;
-  args.rope = g->d_rope;
-  args.pos_div = ax.pos_div;
-  args.pos_mod = ax.pos_mod;
-  args.rope_cols = 2 * kDimInner;
-  args.gate_b = w.gate_b;
-  args.gates_out = g->gates;
-  if (!launched(g, launch_gemm(kEpiQkvRope, bf, maps, args, g->sm_count, g->stream), "qkv gemm")) return false;
-
-  CUtensorMap q4;
-  const uint64_t dims[4] = {static_cast<uint64_t>(kQkvDim), static_cast<uint64_t>(ax.d1),
-                            static_cast<uint64_t>(ax.d2), static_cast<uint64_t>(ax.d3)};
-  const uint64_t row_bytes = kQkvDim * 2ull;
-  const uint64_t strides[3] = {row_bytes, row_bytes * ax.d1, row_bytes * ax.d1 * ax.d2};
-  const uint32_t box[4] = {64u, ax.pos_dim == 1 ? 128u : 1u, ax.pos_dim == 2 ? 128u : 1u, 1u};
-  if (!make_tmap_4d(&q4, g->qkv, 2, dims, strides, box, bf)) return false;
-  AttnArgs at;
-  at.length = ax.length;
-  at.sequences = ax.sequences;
-  at.q_tiles = (ax.length + 127) / 128;
-  at.pos_dim = ax.pos_dim;
-  at.d1 = ax.d1;
-  at.d2 = ax.d2;
-  at.gates = g->gates;
-  at.out = g->attn;
-  at.err = g->d_err;
-  if (!launched(g, launch_attention(bf, q4, at, g->sm_count, g->stream), ax.length <= 128 ? "attention (L<=128)" : "attention (L>128)"))
-    return false;
-
-  // x += out(attn); x16 and row_inv of the new x
-  if (!make_map_rows(g, &maps.a, g->attn, tokens, kDimInner, 128) || !make_resid_maps(g, maps, tokens)) return false;
-  maps.b = w.m_out;
-  args = uniform_args(g, tokens, kDim, kDimInner);
-  args.row_inv_out = g->row_inv;
-  if (!launched(g, launch_gemm(kEpiResidual, bf, maps, args, g->sm_count, g->stream), "out gemm")) return false;
-
-  // hidden = GELU(inv * x16 (ff_gamma o W1)^T + b1)
-  if (!make_map_rows(g, &maps.a, g->x16, tokens, kDim, 128) || !make_out16_map(g, &maps.c, g->qkv, tokens, kFfDim))
-    return false;
-  maps.b = w.m_ff1;
-  maps.d = maps.c;
-  args = uniform_args(g, tokens, kFfDim, kDim);
-  args.row_inv = g->row_inv;
-  args.bias = w.ff1_b;
-  if (!launched(g, launch_gemm(kEpiGelu, bf, maps, args, g->sm_count, g->stream), "ff1 gemm")) return false;
-
-  // x += hidden W2^T + b2; x16 and row_inv of the new x
-  if (!make_map_rows(g, &maps.a, g->qkv, tokens, kFfDim, 128) || !make_resid_maps(g, maps, tokens)) return false;
-  maps.b = w.m_ff2;
-  args = uniform_args(g, tokens, kDim, kFfDim);
-  args.bias = w.ff2_b;
-  args.row_inv_out = g->row_inv;
-  if (!launched(g, launch_gemm(kEpiResidual, bf, maps, args, g->sm_count, g->stream), "ff2 gemm")) return false;
   g->stats_valid = 1;
   return true;
 }

@@ -97,9 +97,6 @@ struct StackBlock {
   CUtensorMap m_qkv, m_out, m_ff1, m_ff2;
 };
 
-struct AxisShape {
-  int pos_dim, d1, d2, d3, sequences, length, pos_div, pos_mod;
-};
 
 }  // namespace
 
@@ -223,10 +220,6 @@ struct SArena {
 bool map_rows(Stack* s, CUtensorMap* map, const void* base, long long rows, int k, int box_rows) {
   return make_tmap_2d(map, base, 2, static_cast<uint64_t>(k), static_cast<uint64_t>(rows),
                       static_cast<uint64_t>(k) * 2, 64, static_cast<uint32_t>(box_rows), 128, s->bf16 != 0);
-}
-bool out16_map(Stack* s, CUtensorMap* map, const void* base, long long rows, int n) {
-  return make_tmap_2d(map, base, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(rows),
-                      static_cast<uint64_t>(n) * 2, 64, 32, 128, s->bf16 != 0);
 }
 
 // 16-bit weight matrix W[rows][k] into the arena, with its B-operand map.
@@ -503,111 +496,26 @@ bool ensure_mask_tiles_s(Stack* s, int frames) {
   return true;
 }
 
-GemmArgs args_for(Stack* s, long long rows, int n, int k) {
-  GemmArgs a;
-  memset(&a, 0, sizeof(a));
-  a.m_rows = static_cast<int>(rows);
-  a.n_tiles = n / 256;
-  a.k_blocks = k / 64;
-  a.num_tiles = static_cast<int>((rows + 127) / 128) * a.n_tiles;
-  a.err = s->d_err;
-  a.pos_div = 1;
-  a.pos_mod = 1;
-  return a;
+bool stack_hook(void* owner, cudaError_t e, const char* what) {
+  return slaunched(static_cast<Stack*>(owner), e, what);
 }
 
-// Residual GEMM x += A B^T (+ bias) with the row statistics of the new x.
-bool residual_gemm(Stack* s, const CUtensorMap& map_a, const CUtensorMap& map_b, long long tokens, int k,
-                   const float* bias, const char* what) {
-  const int d = s->shape.dim;
-  GemmMaps maps;
-  maps.a = map_a;
-  maps.b = map_b;
-  if (!make_tmap_2d(&maps.c, s->x, 4, d, static_cast<uint64_t>(tokens), d * 4ull, 32, 32, 128, false) ||
-      !make_tmap_2d(&maps.d, s->x16, 2, d, static_cast<uint64_t>(tokens), d * 2ull, 32, 32, 64, s->bf16 != 0))
-    return false;
-  GemmArgs args = args_for(s, tokens, d, k);
-  args.bias = bias;
-  if (d == 256) {
-    args.row_inv_out = s->row_inv;
-    return slaunched(s, launch_gemm(kEpiResidual, s->bf16 != 0, maps, args, s->sm_count, s->stream), what);
-  }
-  args.row_sumsq_out = s->sumsq;
-  return slaunched(s, launch_gemm(kEpiResidual, s->bf16 != 0, maps, args, s->sm_count, s->stream), what) &&
-         slaunched(s, launch_norm_finalize(s->sumsq, s->row_inv, tokens, sqrtf(static_cast<float>(d)), s->stream),
-                   "norm finalize");
-}
-
-// One axial block on s->x (x16 / row_inv describe the current x and are left
-// describing the updated x).
-bool run_block_s(Stack* s, const StackBlock& w, long long tokens, const AxisShape& ax) {
+// One axial block on s->x through the shared orchestration of block.cu
+// (x16 / row_inv describe the current x and are left describing the updated x).
+bool run_block_s(Stack* s, const StackBlock& w, long long tokens, const AxisPlan& ax) {
   const StackShape& sh = s->shape;
-  const bool bf = s->bf16 != 0;
-  const int d = sh.dim;
   if (!ensure_rope_s(s, ax.length)) return false;
-  GemmMaps maps;
-  if (!map_rows(s, &maps.a, s->x16, tokens, d, 128) || !out16_map(s, &maps.c, s->wide, tokens, kQkvDim)) return false;
-  maps.b = w.m_qkv;
-  maps.d = maps.c;
-  GemmArgs args = args_for(s, tokens, kQkvDim, d);
-  args.gate_tile = 1;
-  args.num_tiles = static_cast<int>((tokens + 127) / 128) * (args.n_tiles + 1);
-  args.row_inv = s->row_inv;
-  args.rope = s->d_rope;
-  args.pos_div = ax.pos_div;
-  args.pos_mod = ax.pos_mod;
-  args.rope_cols = 2 * kDimInner;
-  args.gate_b = w.gate_b;
-  args.gates_out = s->gates;
-  if (!slaunched(s, launch_gemm(kEpiQkvRope, bf, maps, args, s->sm_count, s->stream), "qkv gemm")) return false;
-
-  CUtensorMap q4;
-  const uint64_t dims[4] = {static_cast<uint64_t>(kQkvDim), static_cast<uint64_t>(ax.d1),
-                            static_cast<uint64_t>(ax.d2), static_cast<uint64_t>(ax.d3)};
-  const uint64_t row_bytes = kQkvDim * 2ull;
-  const uint64_t strides[3] = {row_bytes, row_bytes * ax.d1, row_bytes * ax.d1 * ax.d2};
-  const uint32_t box[4] = {64u, ax.pos_dim == 1 ? 128u : 1u, ax.pos_dim == 2 ? 128u : 1u, 1u};
-  if (!make_tmap_4d(&q4, s->wide, 2, dims, strides, box, bf)) return false;
-  AttnArgs at;
-  at.length = ax.length;
-  at.sequences = ax.sequences;
-  at.q_tiles = (ax.length + 127) / 128;
-  at.pos_dim = ax.pos_dim;
-  at.d1 = ax.d1;
-  at.d2 = ax.d2;
-  at.gates = s->gates;
-  at.out = s->attn;
-  at.err = s->d_err;
-  if (!slaunched(s, launch_attention(bf, q4, at, s->sm_count, s->stream),
-                 ax.length <= 128 ? "attention (L<=128)" : "attention (L>128)"))
-    return false;
-
-  CUtensorMap a_attn, a_x16, a_hidden;
-  if (!map_rows(s, &a_attn, s->attn, tokens, kDimInner, 128) ||
-      !residual_gemm(s, a_attn, w.m_out, tokens, kDimInner, nullptr, "out gemm"))
-    return false;
-
-  // FFN input projection on the normed x: GELU, or GEGLU over interleaved pairs.
-  if (!map_rows(s, &a_x16, s->x16, tokens, d, 128) || !out16_map(s, &maps.c, s->wide, tokens, sh.ff_inner))
-    return false;
-  maps.a = a_x16;
-  maps.b = w.m_ff1;
-  maps.d = maps.c;
-  args = args_for(s, tokens, sh.ff1_rows, d);
-  args.row_inv = s->row_inv;
-  args.bias = w.ff1_b;
-  if (!slaunched(s, launch_gemm(sh.geglu ? kEpiGeglu : kEpiGelu, bf, maps, args, s->sm_count, s->stream), "ff1 gemm"))
-    return false;
-
-  return map_rows(s, &a_hidden, s->wide, tokens, sh.ff_inner, 128) &&
-         residual_gemm(s, a_hidden, w.m_ff2, tokens, sh.ff_inner, w.ff2_b, "ff2 gemm");
+  const AxialBuffers buf{s->x, s->x16, s->row_inv, s->sumsq, s->wide, s->attn, s->gates, s->d_rope, s->d_err};
+  const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.gate_b, w.ff1_b, w.ff2_b};
+  return run_axial_block(buf, aw, AxialShape{sh.dim, sh.ff_inner, sh.geglu}, tokens, ax, s->bf16 != 0, s->sm_count,
+                         s->stream, stack_hook, s);
 }
 
-AxisShape time_axis_s(const StackShape& sh, int clips, int frames) {
-  return AxisShape{1, frames, sh.bands, clips, clips * sh.bands, frames, 1, frames};
+AxisPlan time_axis_s(const StackShape& sh, int clips, int frames) {
+  return AxisPlan{1, frames, sh.bands, clips, clips * sh.bands, frames, 1, frames};
 }
-AxisShape band_axis_s(const StackShape& sh, int clips, int frames) {
-  return AxisShape{2, frames, sh.bands, clips, clips * frames, sh.bands, frames, sh.bands};
+AxisPlan band_axis_s(const StackShape& sh, int clips, int frames) {
+  return AxisPlan{2, frames, sh.bands, clips, clips * frames, sh.bands, frames, sh.bands};
 }
 
 // Row statistics of the band-split output (later ones come from the residual
@@ -823,7 +731,7 @@ int vocalarc_b200_stack_stage_block(vocalarc_b200_stack* s, float* d_x, int clip
   if (!sok(s, cudaMemcpyAsync(s->x, d_x, bytes, cudaMemcpyDeviceToDevice, s->stream), "stage copy") ||
       !row_stats_s(s, tokens))
     return 0;
-  const AxisShape ax = axis == 0 ? time_axis_s(sh, clips, frames) : band_axis_s(sh, clips, frames);
+  const AxisPlan ax = axis == 0 ? time_axis_s(sh, clips, frames) : band_axis_s(sh, clips, frames);
   if (!run_block_s(s, s->blocks[static_cast<size_t>(2 * layer + axis)], tokens, ax)) return 0;
   return sok(s, cudaMemcpyAsync(d_x, s->x, bytes, cudaMemcpyDeviceToDevice, s->stream), "stage copy") ? 1 : 0;
 }

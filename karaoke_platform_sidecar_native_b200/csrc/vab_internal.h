@@ -196,6 +196,49 @@ cudaError_t launch_demix_range(const float* seg_out, SegmentMap map, int chunks,
 cudaError_t launch_tta_inputs(const float* mix, int n, int shifts, int variants, float* out, cudaStream_t stream);
 cudaError_t launch_tta_combine(const float* est, int n, int shifts, int tta, float* vocals, cudaStream_t stream);
 cudaError_t launch_transpose_tokens(const float* src, float* dst, int s0, int l0, cudaStream_t stream);
+// ---- one axial block (block.cu), shared by the provider and the configurable stack
+// Token grid (d1, d2, d3): row = (i3 * d2 + i2) * d1 + i1.  Attention runs
+// along dim `pos_dim` over `sequences` sequences of `length` tokens; the RoPE
+// position of row r is (r / pos_div) % pos_mod.
+struct AxisPlan {
+  int pos_dim, d1, d2, d3, sequences, length, pos_div, pos_mod;
+};
+// B-operand maps and vectors of one block's weights (norm gammas folded in).
+struct AxialWeights {
+  const CUtensorMap* m_qkv;
+  const CUtensorMap* m_out;
+  const CUtensorMap* m_ff1;
+  const CUtensorMap* m_ff2;
+  const float* gate_b;
+  const float* ff1_b;
+  const float* ff2_b;
+};
+// The residual stream (fp32 x, its 16-bit copy, the per-row RMSNorm factor)
+// and the block's operand buffers; `wide` holds q|k|v [tokens][1536], later
+// the FFN hidden.  sumsq: width > 256 only (zero between uses).
+struct AxialBuffers {
+  float* x;
+  void* x16;
+  float* row_inv;
+  float* sumsq;
+  void* wide;
+  void* attn;
+  float* gates;
+  const float2* rope;
+  int* err;
+};
+struct AxialShape {
+  int dim;        // 256 or 512
+  int ff_inner;   // FFN hidden width
+  int geglu;      // 1: the FFN input GEMM emits interleaved (value, gate) rows
+};
+// The owner's launch bookkeeping (error check, launch count, trace mark).
+using LaunchHook = bool (*)(void* owner, cudaError_t e, const char* what);
+// Needs x16 / row_inv of the current x and the RoPE table for ax.length
+// positions; leaves them describing the updated x.
+bool run_axial_block(const AxialBuffers& b, const AxialWeights& w, const AxialShape& sh, long long tokens,
+                     const AxisPlan& ax, bool bf16, int sm_count, cudaStream_t stream, LaunchHook hook, void* owner);
+
 // One CTA waiting, with the kernels' wait loop and the given limit, on an
 // mbarrier that never completes; records kErrWaitTma in *err and returns.
 cudaError_t launch_wait_check(int* err, unsigned long long limit_ns, cudaStream_t stream);
