@@ -14,8 +14,6 @@
 // operand).  Warps 2-9, one thread per query row, read S from TMEM, compute
 // the softmax in fp32 with exp2 and write P (16-bit) to 128-byte-swizzled
 // shared memory.
-#include <type_traits>
-
 #include "ptx.cuh"
 #include "vab_internal.h"
 
@@ -61,44 +59,6 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   p = __ffma2_rn(p, f, make_float2(0.9999281764030457f, 0.9999281764030457f));
   return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
                      __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
-}
-
-// 2^x for a pair of fp16 values on MUFU in packed form: two results per
-// instruction, returned as the packed 16-bit pair itself.
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-// Exponentials of one 64-column half of a score row for fp16 operands:
-// x = s c - m c in fp32 pairs, rounded to f16x2 (|x| <= 8 above the reference
-// maximum, so the rounding moves 2^x by at most 2^-9 ln 2 relative) and
-// exponentiated in packed form, which gives the 16-bit P operand directly
-// (one MUFU instruction and one conversion per pair instead of two MUFU
-// instructions, a conversion and an add).  The row sum adds the same rounded
-// P values that the PV MMA uses: f16x2 sums of groups of four pairs (at most 8
-// values of at most 2^8 each) are accumulated in fp32.
-__device__ __forceinline__ float softmax_half_f16(const float (&v)[64], float mscaled, uint32_t* pk) {
-  const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
-  const float2 nm2 = make_float2(-mscaled, -mscaled);
-  float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    __half2 hs[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int q = g * 8 + 2 * i;
-      const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
-      const __half2 hx = __float22half2_rn(x2);
-      const uint32_t p = ex2_f16x2(*reinterpret_cast<const uint32_t*>(&hx));
-      pk[g * 4 + i] = p;
-      hs[i] = *reinterpret_cast<const __half2*>(&p);
-    }
-    const __half2 sg = __hadd2(__hadd2(hs[0], hs[1]), __hadd2(hs[2], hs[3]));
-    acc = __fadd2_rn(acc, __half22float2(sg));
-  }
-  return acc.x + acc.y;
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -448,29 +408,25 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             }
           }
           const float mscaled = m_ref * kScaleLog2;
-          if constexpr (std::is_same<T, __half>::value) {
-            sum += softmax_half_f16(v, mscaled, pk + 32 * hh);
-          } else {
-            const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
-            const float2 nm2 = make_float2(-mscaled, -mscaled);
-            float2 sums[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                              make_float2(0.f, 0.f)};
+          const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
+          const float2 nm2 = make_float2(-mscaled, -mscaled);
+          float2 sums[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                            make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int q = 0; q < 64; q += 2) {
-              const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
-              float2 p2;
-              if (((q >> 1) & 7) < kPolyPairs) {
-                p2 = exp2_poly2(x2);
-              } else {
-                p2.x = ex2_approx(x2.x);
-                p2.y = ex2_approx(x2.y);
-              }
-              sums[(q >> 1) & 3] = __fadd2_rn(sums[(q >> 1) & 3], p2);
-              pk[32 * hh + q / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
+          for (int q = 0; q < 64; q += 2) {
+            const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
+            float2 p2;
+            if (((q >> 1) & 7) < kPolyPairs) {
+              p2 = exp2_poly2(x2);
+            } else {
+              p2.x = ex2_approx(x2.x);
+              p2.y = ex2_approx(x2.y);
             }
-            const float2 s01 = __fadd2_rn(__fadd2_rn(sums[0], sums[1]), __fadd2_rn(sums[2], sums[3]));
-            sum += s01.x + s01.y;
+            sums[(q >> 1) & 3] = __fadd2_rn(sums[(q >> 1) & 3], p2);
+            pk[32 * hh + q / 2] = ElemTraits<T>::pack2(p2.x, p2.y);
           }
+          const float2 s01 = __fadd2_rn(__fadd2_rn(sums[0], sums[1]), __fadd2_rn(sums[2], sums[3]));
+          sum += s01.x + s01.y;
         }
         const bool raise = raised;
         if (c > 0) {
