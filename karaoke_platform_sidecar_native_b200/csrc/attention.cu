@@ -538,7 +538,9 @@ cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, int sm_cou
 // Short sequences (L <= 128, the band axis: L = 90): a persistent CTA walks
 // (sequence, head) items.  The kernel moves about 46 KB per item (q, k, v in,
 // gated output out), so the design keeps loads in flight and every stage busy:
-// four shared-memory stages of Q, K, V run ahead of the MMAs; items alternate
+// Q and K (freed when S = Q K^T completes) and V (freed when O = P V completes)
+// have rings of their own, four stages each, filled by two loader warps, so a
+// stage is held only for as long as its operand is needed; items alternate
 // between two softmax warp groups (warps 2-5: group 0, warps 6-9: group 1),
 // each with one TMEM S buffer (P written over it) and two O buffers, and a
 // group writes an item's output only after the softmax of its next item, so
@@ -546,15 +548,16 @@ cudaError_t launch_pair(const CUtensorMap& map, const AttnArgs& args, int sm_cou
 // warp whose 32 rows all lie at or past the sequence length (rows 96-127 for
 // L = 90) does no softmax or output work: the rows of P it leaves stale only
 // reach rows of O that are never stored.
-constexpr int kItemThreads = 352;   // warps: TMA, S issuer, 8 softmax, PV issuer
-constexpr int kItemStages = 3;
+constexpr int kItemThreads = 384;   // warps: Q/K loader, S issuer, 8 softmax, PV issuer, V loader
+constexpr int kItemStages = 4;      // stages of each ring
 
 struct ItemSmem {
-  static constexpr int kStage = 3 * kQBytes;           // Q, K, V: 48 KB
-  static constexpr int kOut = kItemStages * kStage;    // per group: the gated output tile, 128 x 64 16-bit
+  static constexpr int kQkStage = 2 * kQBytes;               // Q, K: 32 KB
+  static constexpr int kV = kItemStages * kQkStage;           // V ring: kItemStages x 16 KB
+  static constexpr int kOut = kV + kItemStages * kQBytes;     // per group: the gated output tile, 128 x 64 16-bit
   static constexpr int kOutBytes = kTile * kDimHead * 2;
   static constexpr int kBar = kOut + 2 * kOutBytes;
-  static constexpr int kBytes = 1024 + kBar + 256;
+  static constexpr int kBytes = 1024 + kBar + 512;
 };
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
@@ -591,9 +594,11 @@ __global__ void __launch_bounds__(kItemThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* full = bars;                             // [stage]
-  uint64_t* stage_free = bars + kItemStages;         // [stage]
-  uint64_t* s_full = bars + 2 * kItemStages;         // [group]
+  uint64_t* qk_full = bars;                          // [stage]
+  uint64_t* qk_free = bars + kItemStages;            // [stage]
+  uint64_t* v_full = bars + 2 * kItemStages;         // [stage]
+  uint64_t* v_free = bars + 3 * kItemStages;         // [stage]
+  uint64_t* s_full = bars + 4 * kItemStages;         // [group]
   uint64_t* p_full = s_full + 2;                     // [group]
   uint64_t* o_full = p_full + 2;                     // [group][buffer]
   uint64_t* o_free = o_full + 4;                     // [group][buffer]
@@ -612,8 +617,10 @@ __global__ void __launch_bounds__(kItemThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kItemStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&stage_free[i], 1);
+      mbar_init(&qk_full[i], 1);
+      mbar_init(&qk_free[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_free[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -643,14 +650,17 @@ __global__ void __launch_bounds__(kItemThreads, 1)
   // Item k of this CTA: global item blockIdx.x + k * gridDim.x; head fastest.
   auto item_of = [&](int k) { return static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x); };
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 11) {
+    // Loaders: warp 0 brings Q and K of each item into the Q/K ring, warp 11
+    // brings V into the V ring; each waits only for its own ring's stage.
     if (lane == 0) {
+      const bool qk = warp == 0;
       tma_prefetch(&map);
-      tma_prefetch(&map_out);
+      if (qk) tma_prefetch(&map_out);
       for (int k = 0; k < n_local; ++k) {
         const int st = k % kItemStages;
         const uint32_t par = static_cast<uint32_t>(k / kItemStages) & 1u;
-        if (!mbar_wait(&stage_free[st], par ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
+        if (!mbar_wait(qk ? &qk_free[st] : &v_free[st], par ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
         const int item = item_of(k);
         const int head = item % kHeads;
         const int seq = item / kHeads;
@@ -662,15 +672,16 @@ __global__ void __launch_bounds__(kItemThreads, 1)
           c_a = seq % args.d1;
           c_b = seq / args.d1;
         }
-        uint8_t* dst = smem + st * L::kStage;
-        mbar_arrive_expect_tx(&full[st], 3 * kQBytes);
-#pragma unroll
-        for (int part = 0; part < 3; ++part) {
+        uint64_t* bar = qk ? &qk_full[st] : &v_full[st];
+        uint8_t* dst = qk ? smem + st * L::kQkStage : smem + L::kV + st * kQBytes;
+        mbar_arrive_expect_tx(bar, qk ? 2 * kQBytes : kQBytes);
+        for (int part = qk ? 0 : 2; part < (qk ? 2 : 3); ++part) {
           const int col = part * kDimInner + head * kDimHead;
+          uint8_t* d = dst + (qk ? part * kQBytes : 0);
           if (args.pos_dim == 1)
-            tma_load_4d(dst + part * kQBytes, &map, &full[st], col, 0, c_a, c_b);
+            tma_load_4d(d, &map, bar, col, 0, c_a, c_b);
           else
-            tma_load_4d(dst + part * kQBytes, &map, &full[st], col, c_a, 0, c_b);
+            tma_load_4d(d, &map, bar, col, c_a, 0, c_b);
         }
       }
     }
@@ -686,7 +697,7 @@ __global__ void __launch_bounds__(kItemThreads, 1)
       const int g = k & 1;
       const int i = k >> 1;
       const int st = k % kItemStages;
-      if (!mbar_wait_warp(&full[st], static_cast<uint32_t>(k / kItemStages) & 1u, abort_flag, args.err,
+      if (!mbar_wait_warp(&qk_full[st], static_cast<uint32_t>(k / kItemStages) & 1u, abort_flag, args.err,
                           kErrWaitMma)) {
         ok = false;
         break;
@@ -698,12 +709,13 @@ __global__ void __launch_bounds__(kItemThreads, 1)
       }
       tc_fence_after();
       if (elect_one()) {
-        const uint64_t qd = base_desc_k + static_cast<uint64_t>((st * L::kStage) >> 4);
+        const uint64_t qd = base_desc_k + static_cast<uint64_t>((st * L::kQkStage) >> 4);
         const uint64_t kd = qd + static_cast<uint64_t>(kQBytes >> 4);
 #pragma unroll
         for (int kk = 0; kk < kDimHead / 16; ++kk)
           umma_f16(tmem_base + g * NCOLS, qd + 2 * kk, kd + 2 * kk, idesc_s, kk != 0 ? 1u : 0u);
         umma_commit(&s_full[g]);
+        umma_commit(&qk_free[st]);   // Q and K of this stage are read
       }
       __syncwarp();
     }
@@ -713,9 +725,8 @@ __global__ void __launch_bounds__(kItemThreads, 1)
     }
     __syncwarp();
   } else if (warp == 10) {
-    // PV issuer: O(k) = P(k) V as soon as item k's P is in TMEM and its O
-    // buffer was read (item k - 4).  PV(k) follows the softmax's read of S(k),
-    // so its commit also covers the Q, K reads of S(k): it frees the stage.
+    // PV issuer: O(k) = P(k) V as soon as item k's P is in TMEM, its V is in
+    // and its O buffer was read (item k - 4); its commit frees the V stage.
     const uint32_t bf = ElemTraits<T>::kBf16;
     const uint32_t idesc_o = idesc_f16(kTile, kDimHead, bf, 0, 1);
     const uint64_t base_desc_v = sw128_desc(smem_u32(smem), 8192, 1024);
@@ -728,9 +739,12 @@ __global__ void __launch_bounds__(kItemThreads, 1)
       if (i >= 2 && !mbar_wait_warp(&o_free[ob], static_cast<uint32_t>((i >> 1) - 1) & 1u, abort_flag, args.err,
                                     kErrWaitMma))
         break;
+      if (!mbar_wait_warp(&v_full[st], static_cast<uint32_t>(k / kItemStages) & 1u, abort_flag, args.err,
+                          kErrWaitMma))
+        break;
       tc_fence_after();
       if (elect_one()) {
-        const uint64_t vd = base_desc_v + static_cast<uint64_t>((st * L::kStage + 2 * kQBytes) >> 4);
+        const uint64_t vd = base_desc_v + static_cast<uint64_t>((L::kV + st * kQBytes) >> 4);
         const uint32_t p_col = tmem_base + g * NCOLS;
 #pragma unroll
         for (int kk = 0; kk < NCOLS / 16; ++kk)
@@ -738,7 +752,7 @@ __global__ void __launch_bounds__(kItemThreads, 1)
             umma_f16_ts(tmem_base + kColO + ob * kDimHead, p_col + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
                         kk != 0 ? 1u : 0u);
         umma_commit(&o_full[ob]);
-        umma_commit(&stage_free[st]);
+        umma_commit(&v_free[st]);
       }
       __syncwarp();
     }
