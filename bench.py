@@ -296,8 +296,12 @@ def reference_gpu_baseline(device, reps=3):
     chunk = fixtures.demix_chunk(fixtures.long_mix(240.0, seed=1), 13)
     out = {"exe": "native/vocalarc_separation.c + native/native_gpu_cuda.cu (cuBLAS), unchanged, sm_100a",
            "device": device, "threads": threads}
+    # The reference build uses device 0 of what it sees: show it only this
+    # process's GPU (an entry of an inherited CUDA_VISIBLE_DEVICES list, if any).
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    own = visible[device] if device < len(visible) else str(device)
     for tf32 in ("1", "0"):
-        env = dict(os.environ, VOCALARC_GPU_TF32=tf32, CUDA_VISIBLE_DEVICES=str(device))
+        env = dict(os.environ, VOCALARC_GPU_TF32=tf32, CUDA_VISIBLE_DEVICES=own)
         replies = []
         res = reference_cpu_run(pack, [clip] * (reps + 1) + [chunk], threads, warmup=1, exe=REF_CUBLAS_EXE, env=env,
                                 replies=replies)
