@@ -179,3 +179,22 @@ def test_separate_files_pipeline(tmp_path, test_pack_blob):
                               fixtures.read_wav_f32(str(vocals[1])))
     finally:
         p.close()
+
+
+def test_separate_files_chunked_mode(tmp_path, test_pack_blob):
+    # chunked = 1: each track goes through the chunked demix, exactly as
+    # vocalarc_b200_separate_chunked separates the decoded input.
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    mix = fixtures.long_mix(1.5, seed=12)
+    src = tmp_path / "in.wav"
+    src.write_bytes(fixtures.wav_bytes(mix, rate=22050, bits=16, pcm=True))
+    out = tmp_path / "v.wav"
+    p = native.Provider(0)
+    try:
+        p.load_model(test_pack_blob)
+        assert p.separate_files([str(src)], [str(out)], chunked=True) == 1
+        decoded = native.read_track(str(src))
+        assert np.array_equal(fixtures.read_wav_f32(str(out)), p.separate_chunked(decoded))
+    finally:
+        p.close()
