@@ -77,6 +77,7 @@ def kernel_work(name, chunks_per_launch):
 
         "ff1 gemm": 2 * tokens * 256 * 1024,
         "ff2 gemm": 2 * tokens * 1024 * 256,
+        "ffn": 2 * 2 * tokens * 256 * 1024,
         "attention (L>128)": 4 * 64 * 8 * (c * 90) * t * t,
         "attention (L<=128)": 4 * 64 * 8 * (c * t) * 90 * 90,
         "mask gemm 1": 2 * tokens * 256 * 1024,

@@ -2,11 +2,14 @@
 // shared by the bundled provider (runtime.cu) and the configurable stack
 // (stack.cu).  transformer_forward, native/vocalarc_separation.c:836-873:
 //   x += Out(Gate(Attn(RoPE(QKV(RMSNorm x)))));  x += FF2(act(FF1(RMSNorm x)))
-// as five launches: the QKV GEMM (RoPE, row scale and the head-gate tile in
+// as four or five launches: the QKV GEMM (RoPE, row scale and the head-gate tile in
 // its epilogue), tcgen05 attention with the gate in its output stage, the
-// out-projection GEMM with the fp32 residual and the new row statistics, the
-// FFN input GEMM (bias + GELU, or GEGLU), and the FFN output GEMM with the
-// residual and row statistics.  RMSNorm gammas are folded into the weights.
+// out-projection GEMM with the fp32 residual and the new row statistics, and
+// the FFN: for width 256 with GELU one fused kernel that keeps the hidden on
+// chip, otherwise the FFN input GEMM (bias + GELU, or GEGLU) and the FFN output
+// GEMM with the residual and row statistics.  RMSNorm gammas are folded into
+// the weights.
+#include <cstdlib>
 #include <cstring>
 
 #include "vab_internal.h"
@@ -36,6 +39,17 @@ GemmArgs block_args(const AxialBuffers& b, long long rows, int n, int k) {
   a.pos_div = 1;
   a.pos_mod = 1;
   return a;
+}
+
+// VOCALARC_B200_FFN=split selects the two-launch FFN (FF1 writes the hidden to
+// HBM, FF2 reads it back) where the fused kernel applies; both compute the same
+// products in the same order per output element up to the hidden's rounding.
+bool ffn_fused_enabled() {
+  static const bool fused = [] {
+    const char* v = getenv("VOCALARC_B200_FFN");
+    return v == nullptr || strcmp(v, "split") != 0;
+  }();
+  return fused;
 }
 
 }  // namespace
@@ -110,6 +124,26 @@ bool run_axial_block(const AxialBuffers& b, const AxialWeights& w, const AxialSh
   if (!rows_map(&a_attn, b.attn, tokens, kDimInner, bf16) ||
       !residual(a_attn, *w.m_out, kDimInner, nullptr, "out gemm"))
     return false;
+
+  // x += GELU(inv * x16 (ff_gamma o W1)^T + b1) W2^T + b2 in one kernel, the
+  // hidden on chip (width 256, GELU).
+  if (d == 256 && !sh.geglu && sh.ff_inner % 128 == 0 && w.ff1_w != nullptr && ffn_fused_enabled()) {
+    FfnMaps fm;
+    if (!rows_map(&fm.x16, b.x16, tokens, d, bf16) ||
+        !make_tmap_2d(&fm.w1, w.ff1_w, 2, d, static_cast<uint64_t>(sh.ff_inner), d * 2ull, 64, 128, 128, bf16) ||
+        !make_tmap_2d(&fm.res, b.x, 4, d, static_cast<uint64_t>(tokens), d * 4ull, 32, 32, 128, false) ||
+        !make_tmap_2d(&fm.out16, b.x16, 2, d, static_cast<uint64_t>(tokens), d * 2ull, 32, 32, 64, bf16))
+      return false;
+    fm.w2 = *w.m_ff2;
+    GemmArgs fa = block_args(b, tokens, d, d);
+    fa.num_tiles = static_cast<int>((tokens + 127) / 128);
+    fa.row_inv = b.row_inv;
+    fa.row_inv_out = b.row_inv;
+    fa.bias1 = w.ff1_b;
+    fa.bias = w.ff2_b;
+    fa.out = b.x;
+    return hook(owner, launch_ffn(bf16, fm, fa, sh.ff_inner, sm_count, stream), "ffn");
+  }
 
   // hidden = GELU(inv * x16 (ff_gamma o W1)^T + b1), or GEGLU over interleaved (value, gate) rows.
   if (!rows_map(&a_x16, b.x16, tokens, d, bf16) || !out16_map(&maps.c, b.wide, tokens, sh.ff_inner, bf16))

@@ -239,24 +239,25 @@ __device__ __forceinline__ void epilogue_out16(const GemmArgs& args, const CUten
 // the other column half through shared memory, inv = sqrt(256)/sqrt(sum + 1e-12)
 // for the row (transformer_forward's residual_add + the following rms_norm's
 // scale, vocalarc_separation.c:864-866, :849, rms_norm_row_scalar :419-424).
+// residual_blocks does the four 32-column blocks of this warp's half and
+// returns the row's partial sum of squares; the caller combines the halves.
 template <typename T>
-__device__ __forceinline__ void epilogue_residual(const GemmArgs& args, const CUtensorMap* map_res,
-                                                  const CUtensorMap* map_x16, const TileInfo& ti, EpiWarp& ew,
-                                                  uint32_t taddr, int half, int quarter, int row, long long R,
-                                                  bool valid, int row0, int parity, float* red) {
+__device__ __forceinline__ float residual_blocks(const GemmArgs& args, const CUtensorMap* map_res,
+                                                 const CUtensorMap* map_x16, int n0, EpiWarp& ew, uint32_t taddr,
+                                                 int half, int row, bool valid, int row0) {
   float ss = 0.f;
   // Prefetch the first residual block of this warp's columns.
   if (ew.lane == 0) {
     bulk_wait_read0();
     mbar_arrive_expect_tx(ew.bar[ew.cur], kStageBuf);
-    tma_load_2d(ew.buf[ew.cur], map_res, ew.bar[ew.cur], ti.n0 + half * 128, row0);
+    tma_load_2d(ew.buf[ew.cur], map_res, ew.bar[ew.cur], n0 + half * 128, row0);
   }
   __syncwarp();
 #pragma unroll 1
   for (int s = 0; s < 4; ++s) {
     const int b = ew.cur;
     const int c = half * 128 + s * 32;
-    const int n = ti.n0 + c;
+    const int n = n0 + c;
     if (ew.lane == 0 && s + 1 < 4) {
       bulk_wait_read0();   // both stores from the other buffer have read it
       mbar_arrive_expect_tx(ew.bar[b ^ 1], kStageBuf);
@@ -324,6 +325,15 @@ __device__ __forceinline__ void epilogue_residual(const GemmArgs& args, const CU
     }
     ew.cur ^= 1;
   }
+  return ss;
+}
+
+template <typename T>
+__device__ __forceinline__ void epilogue_residual(const GemmArgs& args, const CUtensorMap* map_res,
+                                                  const CUtensorMap* map_x16, const TileInfo& ti, EpiWarp& ew,
+                                                  uint32_t taddr, int half, int quarter, int row, long long R,
+                                                  bool valid, int row0, int parity, float* red) {
+  const float ss = residual_blocks<T>(args, map_res, map_x16, ti.n0, ew, taddr, half, row, valid, row0);
   float* slot = red + (parity * 2 + half) * 128;
   slot[row] = ss;
   named_barrier(1 + quarter, 64);
@@ -682,6 +692,397 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- fused FFN
+// x += GELU(inv * x16 W1^T + b1) W2^T + b2 for a 128-row tile, the hidden
+// activations kept on chip (transformer_forward's FFN, vocalarc_separation.c:
+// 866-873, with the RMSNorm gamma folded into W1).  Per tile:
+//   * the tile's x16 (128 x 256, four K-blocks) stays in shared memory while
+//     all hidden slices are computed;
+//   * the hidden units run in slices of 128: FF1(s) accumulates into one of two
+//     128-column TMEM buffers, the eight epilogue warps apply the row scale,
+//     b1 and GELU and write the 16-bit slice into one of two shared-memory
+//     buffers in the 128B-swizzled K-major layout of an MMA operand, and FF2(s)
+//     accumulates that slice times W2[:, slice] into the 256-column output
+//     accumulator;
+//   * the MMA warp issues FF1(0), FF1(1), FF2(0), FF1(2), FF2(1), ... so the
+//     tensor cores run FF1(s+1) and FF2(s-1) while GELU(s) is computed;
+//   * W1 and W2 stream through one ring of 32 KB stages (two 128 x 64 W1
+//     K-blocks, or one 256 x 64 W2 K-block) in the MMA's order;
+//   * the output tile goes through the residual epilogue of the plain GEMM,
+//     staged in the two hidden buffers, which are free once FF2 of the last
+//     slice has completed.
+// HBM traffic per row: x16 in, x in and out, x16 out (3 KB) instead of the
+// 7 KB of an FF1 launch writing the hidden and an FF2 launch reading it.
+namespace ffn {
+constexpr int kSliceN = 128;
+constexpr int kXBytes = 4 * kABytes;   // 64 KB
+constexpr int kHBytes = 2 * kABytes;   // 32 KB
+constexpr int kWStage = 32768;
+constexpr int kWStages = 3;
+constexpr int kRed = 2 * 128 * 4;      // one column half's row sums, two tile parities
+constexpr int kBarCount = 40;
+constexpr int kSmemBytes = 1024 + kXBytes + 2 * kHBytes + kWStages * kWStage + kRed + kBarBytes;
+static_assert(kSmemBytes <= 232448, "fused FFN shared memory");
+static_assert(kEpiWarps * 2 * kStageBuf == 2 * kHBytes, "residual staging is the two hidden buffers");
+static_assert(kBarCount * 8 + 8 <= kBarBytes, "barrier block");
+}  // namespace ffn
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    ffn_kernel(const __grid_constant__ CUtensorMap map_x16, const __grid_constant__ CUtensorMap map_w1,
+               const __grid_constant__ CUtensorMap map_w2, const __grid_constant__ CUtensorMap map_res,
+               const __grid_constant__ CUtensorMap map_out16, const GemmArgs args, const int slices) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sX = smem;
+  uint8_t* sH = sX + ffn::kXBytes;   // [2][kHBytes]; the residual staging at the tile's end
+  uint8_t* sW = sH + 2 * ffn::kHBytes;
+  float* red = reinterpret_cast<float*>(sW + ffn::kWStages * ffn::kWStage);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + ffn::kRed);
+  uint64_t* x_full = bars + 0;
+  uint64_t* x_free = bars + 1;
+  uint64_t* w_full = bars + 2;       // [3]
+  uint64_t* w_empty = bars + 5;      // [3]
+  uint64_t* acc1_full = bars + 8;    // [2]
+  uint64_t* acc1_empty = bars + 10;  // [2]
+  uint64_t* h_full = bars + 12;      // [2]
+  uint64_t* h_free = bars + 14;      // [2]
+  uint64_t* acc2_full = bars + 16;
+  uint64_t* acc2_empty = bars + 17;
+  uint64_t* stage_free = bars + 18;
+  uint64_t* red_full = bars + 19;    // [4]
+  uint64_t* drain = bars + 23;
+  uint64_t* ep_bar = bars + 24;      // [8 warps][2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + ffn::kBarCount);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    mbar_init(x_full, 1);
+    mbar_init(x_free, 1);
+    for (int s = 0; s < ffn::kWStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc1_full[b], 1);
+      mbar_init(&acc1_empty[b], kEpiWarps);
+      mbar_init(&h_full[b], kEpiWarps);
+      mbar_init(&h_free[b], 1);
+    }
+    mbar_init(acc2_full, 1);
+    mbar_init(acc2_empty, kEpiWarps);
+    mbar_init(stage_free, kEpiWarps);
+    for (int q = 0; q < 4; ++q) mbar_init(&red_full[q], 32);
+    mbar_init(drain, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&ep_bar[i], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&map_x16);
+    tma_prefetch(&map_w1);
+    tma_prefetch(&map_w2);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: x16 per tile, then W1 / W2 stages in the MMA's order.
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t last_phase[ffn::kWStages] = {0, 0, 0};
+      bool used[ffn::kWStages] = {false, false, false};
+      int x_loads = 0;
+      bool ok = true;
+      auto next_stage = [&]() -> bool {
+        if (!mbar_wait(&w_empty[stage], phase ^ 1u, abort_flag, args.err, kErrWaitTma)) return false;
+        mbar_arrive_expect_tx(&w_full[stage], ffn::kWStage);
+        used[stage] = true;
+        last_phase[stage] = phase;
+        return true;
+      };
+      auto advance = [&]() {
+        if (++stage == ffn::kWStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      };
+      auto load_w1 = [&](int s) -> bool {
+        for (int j = 0; j < 2; ++j) {
+          if (!next_stage()) return false;
+          uint8_t* dst = sW + stage * ffn::kWStage;
+          tma_load_2d(dst, &map_w1, &w_full[stage], (2 * j) * kBK, s * ffn::kSliceN);
+          tma_load_2d(dst + kABytes, &map_w1, &w_full[stage], (2 * j + 1) * kBK, s * ffn::kSliceN);
+          advance();
+        }
+        return true;
+      };
+      auto load_w2 = [&](int s) -> bool {
+        for (int j = 0; j < 2; ++j) {
+          if (!next_stage()) return false;
+          tma_load_2d(sW + stage * ffn::kWStage, &map_w2, &w_full[stage], s * ffn::kSliceN + j * kBK, 0);
+          advance();
+        }
+        return true;
+      };
+      int it = 0;
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++it) {
+        const int a_row = tile * kBM;
+        if (!mbar_wait(x_free, (static_cast<uint32_t>(it) & 1u) ^ 1u, abort_flag, args.err, kErrWaitTma)) break;
+        mbar_arrive_expect_tx(x_full, ffn::kXBytes);
+        for (int kb = 0; kb < 4; ++kb) tma_load_2d(sX + kb * kABytes, &map_x16, x_full, kb * kBK, a_row);
+        ++x_loads;
+        // The tile's fp32 residual rows (contiguous, 1 KB each) into L2 for the epilogue.
+        const int rows = min(kBM, args.m_rows - a_row);
+        prefetch_l2_bulk(static_cast<const float*>(args.out) + static_cast<long long>(a_row) * 256,
+                         static_cast<uint32_t>(rows) * 1024u);
+        ok = load_w1(0) && (slices < 2 || load_w1(1));
+        for (int s = 0; s < slices && ok; ++s) ok = load_w2(s) && (s + 2 >= slices || load_w1(s + 2));
+      }
+      // Every load issued has landed before the CTA can exit.
+      if (x_loads > 0) wait_no_abort_check(x_full, static_cast<uint32_t>(x_loads - 1) & 1u, args.err);
+      for (int s = 0; s < ffn::kWStages; ++s)
+        if (used[s]) wait_no_abort_check(&w_full[s], last_phase[s], args.err);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (one elected lane of a converged warp)
+    const uint32_t idesc1 = idesc_f16(kBM, ffn::kSliceN, ElemTraits<T>::kBf16, 0, 0);
+    const uint32_t idesc2 = idesc_f16(kBM, kBN, ElemTraits<T>::kBf16, 0, 0);
+    const uint64_t x_desc0 = sw128_desc(smem_u32(sX), 16, 1024);
+    const uint64_t h_desc0 = sw128_desc(smem_u32(sH), 16, 1024);
+    const uint64_t w_desc0 = sw128_desc(smem_u32(sW), 16, 1024);
+    int stage = 0;
+    uint32_t phase = 0;
+    int g1 = 0, g2 = 0;   // FF1 / FF2 slices issued so far
+    auto wait_stage = [&]() -> bool {
+      if (!mbar_wait_warp(&w_full[stage], phase, abort_flag, args.err, kErrWaitMma)) return false;
+      tc_fence_after();
+      return true;
+    };
+    auto advance = [&]() {
+      if (++stage == ffn::kWStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    };
+    auto issue_ff1 = [&]() -> bool {
+      const int b = g1 & 1;
+      if (!mbar_wait_warp(&acc1_empty[b], (static_cast<uint32_t>(g1 >> 1) & 1u) ^ 1u, abort_flag, args.err,
+                          kErrWaitMma))
+        return false;
+      tc_fence_after();
+      const uint32_t d = tmem_base + static_cast<uint32_t>(kBN + ffn::kSliceN * b);
+      for (int j = 0; j < 2; ++j) {
+        if (!wait_stage()) return false;
+        if (elect_one()) {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint64_t da = x_desc0 + static_cast<uint64_t>(((2 * j + i) * kABytes) >> 4);
+            const uint64_t db = w_desc0 + static_cast<uint64_t>((stage * ffn::kWStage + i * kABytes) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16(d, da + 2 * kk, db + 2 * kk, idesc1, (j | i | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&w_empty[stage]);
+        }
+        __syncwarp();
+        advance();
+      }
+      if (elect_one()) umma_commit(&acc1_full[b]);
+      __syncwarp();
+      ++g1;
+      return true;
+    };
+    auto issue_ff2 = [&](int s) -> bool {
+      const int b = g2 & 1;
+      if (!mbar_wait_warp(&h_full[b], static_cast<uint32_t>(g2 >> 1) & 1u, abort_flag, args.err, kErrWaitMma))
+        return false;
+      tc_fence_after();
+      for (int j = 0; j < 2; ++j) {
+        if (!wait_stage()) return false;
+        if (elect_one()) {
+          const uint64_t da = h_desc0 + static_cast<uint64_t>((b * ffn::kHBytes + j * kABytes) >> 4);
+          const uint64_t db = w_desc0 + static_cast<uint64_t>((stage * ffn::kWStage) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(tmem_base, da + 2 * kk, db + 2 * kk, idesc2, (s | j | kk) != 0 ? 1u : 0u);
+          umma_commit(&w_empty[stage]);
+        }
+        __syncwarp();
+        advance();
+      }
+      if (elect_one()) umma_commit(&h_free[b]);
+      __syncwarp();
+      ++g2;
+      return true;
+    };
+    auto release_x = [&]() {
+      if (elect_one()) umma_commit(x_free);
+      __syncwarp();
+    };
+    int it = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++it) {
+      if (!mbar_wait_warp(x_full, static_cast<uint32_t>(it) & 1u, abort_flag, args.err, kErrWaitMma)) break;
+      tc_fence_after();
+      bool ok = issue_ff1() && (slices < 2 || issue_ff1());
+      if (ok && slices <= 2) release_x();
+      // FF2(0) overwrites the output accumulator: the previous tile's epilogue has read it.
+      ok = ok && mbar_wait_warp(acc2_empty, (static_cast<uint32_t>(it) & 1u) ^ 1u, abort_flag, args.err, kErrWaitMma);
+      if (ok) tc_fence_after();
+      for (int s = 0; s < slices && ok; ++s) {
+        ok = issue_ff2(s);
+        if (ok && s + 2 < slices) {
+          ok = issue_ff1();
+          if (ok && s + 2 == slices - 1) release_x();
+        }
+      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(acc2_full);
+      __syncwarp();
+    }
+    if (elect_one()) {
+      umma_commit(drain);
+      wait_no_abort_check(drain, 0, args.err);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps 2..9: lane quarter warp % 4, column half
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const int ew_index = warp - 2;
+    EpiWarp ew;
+    ew.buf[0] = sH + ew_index * 2 * kStageBuf;
+    ew.buf[1] = ew.buf[0] + kStageBuf;
+    ew.bar[0] = &ep_bar[ew_index * 2];
+    ew.bar[1] = &ep_bar[ew_index * 2 + 1];
+    ew.phase[0] = ew.phase[1] = 0;
+    ew.cur = 0;
+    ew.lane = lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    int g = 0;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++it) {
+      const int a_row = tile * kBM;
+      const long long R = static_cast<long long>(a_row) + row;
+      const bool valid = row < args.m_rows - a_row;
+      // A plain load: this kernel rewrites the same rows' factor at the tile's end.
+      const float inv = valid ? args.row_inv[R] : 1.0f;
+      const float2 inv2 = make_float2(inv, inv);
+      bool ok = true;
+      for (int s = 0; s < slices; ++s, ++g) {
+        const int b = g & 1;
+        const uint32_t gp = static_cast<uint32_t>(g >> 1) & 1u;
+        if (!mbar_wait_warp(&acc1_full[b], gp, abort_flag, args.err, kErrWaitEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t r[2][32];
+        const uint32_t taddr = lane_base + static_cast<uint32_t>(kBN + ffn::kSliceN * b + 64 * half);
+        tmem_ld32(taddr, r[0]);
+        tmem_ld32(taddr + 32, r[1]);
+        tmem_wait_ld();
+        reg_fence(r[0]);
+        reg_fence(r[1]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc1_empty[b]);
+        // The hidden buffer is free once FF2 of slice g - 2 has read it, and
+        // at a tile's first slice once the previous tile's output stores have
+        // read the staging.
+        if (!mbar_wait_warp(&h_free[b], gp ^ 1u, abort_flag, args.err, kErrWaitEpilogue) ||
+            (s == 0 && !mbar_wait_warp(stage_free, (static_cast<uint32_t>(it) & 1u) ^ 1u, abort_flag, args.err,
+                                       kErrWaitEpilogue))) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = sH + b * ffn::kHBytes + half * kABytes;
+        const float* b1 = args.bias1 + s * ffn::kSliceN + 64 * half;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float v[32];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 bv = __ldg(reinterpret_cast<const float4*>(b1 + 32 * hh) + q);
+            const float2 lo = __ffma2_rn(make_float2(__uint_as_float(r[hh][4 * q]), __uint_as_float(r[hh][4 * q + 1])),
+                                         inv2, make_float2(bv.x, bv.y));
+            const float2 hi = __ffma2_rn(
+                make_float2(__uint_as_float(r[hh][4 * q + 2]), __uint_as_float(r[hh][4 * q + 3])), inv2,
+                make_float2(bv.z, bv.w));
+            const float2 g0 = gelu_pair(lo);
+            const float2 g1 = gelu_pair(hi);
+            v[4 * q] = g0.x;
+            v[4 * q + 1] = g0.y;
+            v[4 * q + 2] = g1.x;
+            v[4 * q + 3] = g1.y;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = ElemTraits<T>::pack2(v[q * 8 + 0], v[q * 8 + 1]);
+            w.y = ElemTraits<T>::pack2(v[q * 8 + 2], v[q * 8 + 3]);
+            w.z = ElemTraits<T>::pack2(v[q * 8 + 4], v[q * 8 + 5]);
+            w.w = ElemTraits<T>::pack2(v[q * 8 + 6], v[q * 8 + 7]);
+            *reinterpret_cast<uint4*>(dst + sw128(row, 4 * hh + q)) = w;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&h_full[b]);
+      }
+      if (!ok) break;
+      if (!mbar_wait_warp(acc2_full, static_cast<uint32_t>(it) & 1u, abort_flag, args.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const float ss = residual_blocks<T>(args, &map_res, &map_out16, 0, ew, lane_base, half, row, valid,
+                                          a_row + quarter * 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc2_empty);
+      // inv of the new row from both column halves' sums of squares.
+      float* slot = red + (it & 1) * 128;
+      if (half == 1) {
+        slot[row] = ss;
+        mbar_arrive(&red_full[quarter]);
+      } else {
+        if (!mbar_wait_warp(&red_full[quarter], static_cast<uint32_t>(it) & 1u, abort_flag, args.err,
+                            kErrWaitEpilogue))
+          break;
+        if (valid) args.row_inv_out[R] = 16.0f / sqrtf(ss + slot[row] + 1.0e-12f);   // sqrtf(256) / sqrtf(sum + 1e-12)
+      }
+      // This warp's output stores have read the staging (part of the hidden buffers).
+      if (lane == 0) {
+        bulk_wait_read0();
+        mbar_arrive(stage_free);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 template <typename T, int EPI>
 cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& args, int sm_count, cudaStream_t stream) {
   static std::atomic<unsigned long long> configured{0};
@@ -714,6 +1115,25 @@ cudaError_t launch_gemm(int epilogue, bool bf16, const GemmMaps& maps, const Gem
                         cudaStream_t stream) {
   return bf16 ? dispatch<__nv_bfloat16>(epilogue, maps, args, sm_count, stream)
               : dispatch<__half>(epilogue, maps, args, sm_count, stream);
+}
+
+cudaError_t launch_ffn(bool bf16, const FfnMaps& maps, const GemmArgs& args, int hidden, int sm_count,
+                       cudaStream_t stream) {
+  if (hidden <= 0 || hidden % ffn::kSliceN != 0) return cudaErrorInvalidValue;
+  static std::atomic<unsigned long long> configured_h{0}, configured_b{0};
+  const cudaError_t e = bf16 ? opt_in_smem(ffn_kernel<__nv_bfloat16>, ffn::kSmemBytes, configured_b)
+                             : opt_in_smem(ffn_kernel<__half>, ffn::kSmemBytes, configured_h);
+  if (e != cudaSuccess) return e;
+  if (args.num_tiles <= 0) return cudaSuccess;
+  const int grid = args.num_tiles < sm_count ? args.num_tiles : sm_count;
+  const int slices = hidden / ffn::kSliceN;
+  if (bf16)
+    ffn_kernel<__nv_bfloat16><<<grid, kThreads, ffn::kSmemBytes, stream>>>(maps.x16, maps.w1, maps.w2, maps.res,
+                                                                           maps.out16, args, slices);
+  else
+    ffn_kernel<__half><<<grid, kThreads, ffn::kSmemBytes, stream>>>(maps.x16, maps.w1, maps.w2, maps.res, maps.out16,
+                                                                   args, slices);
+  return cudaGetLastError();
 }
 
 cudaError_t upload_band_tables(const int* first, const int* dims) {

@@ -603,7 +603,7 @@ bool provider_hook(void* owner, cudaError_t e, const char* what) {
 bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan& ax) {
   if (!ensure_rope(g, ax.length) || !ensure_stats(g, tokens)) return false;
   const AxialBuffers buf{g->x, g->x16, g->row_inv, nullptr, g->qkv, g->attn, g->gates, g->d_rope, g->d_err};
-  const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.gate_b, w.ff1_b, w.ff2_b};
+  const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.ff1, w.gate_b, w.ff1_b, w.ff2_b};
   if (!run_axial_block(buf, aw, AxialShape{kDim, kFfDim, 0}, tokens, ax, g->bf16 != 0, g->sm_count, g->stream,
                        provider_hook, g))
     return false;

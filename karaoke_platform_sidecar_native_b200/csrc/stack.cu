@@ -506,7 +506,7 @@ bool run_block_s(Stack* s, const StackBlock& w, long long tokens, const AxisPlan
   const StackShape& sh = s->shape;
   if (!ensure_rope_s(s, ax.length)) return false;
   const AxialBuffers buf{s->x, s->x16, s->row_inv, s->sumsq, s->wide, s->attn, s->gates, s->d_rope, s->d_err};
-  const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.gate_b, w.ff1_b, w.ff2_b};
+  const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.ff1, w.gate_b, w.ff1_b, w.ff2_b};
   return run_axial_block(buf, aw, AxialShape{sh.dim, sh.ff_inner, sh.geglu}, tokens, ax, s->bf16 != 0, s->sm_count,
                          s->stream, stack_hook, s);
 }

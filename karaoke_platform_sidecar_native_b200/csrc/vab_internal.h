@@ -95,6 +95,8 @@ struct GemmArgs {
   int bands;
   const int* band_first;
   const int* band_dim;
+  // launch_ffn: the FFN input bias b1 (bias = the output bias b2).
+  const float* bias1;
 };
 
 // Grouped-tile metadata packing: m_valid (8 bits) | n_size (9 bits) << 8 | band << 17.
@@ -114,6 +116,20 @@ bool make_tmap_4d(CUtensorMap* map, const void* base, int elem_bytes, const uint
 // epilogue.  A and B are 16-bit (f16 or bf16 per `bf16`).
 cudaError_t launch_gemm(int epilogue, bool bf16, const GemmMaps& maps, const GemmArgs& args, int sm_count,
                         cudaStream_t stream);
+
+// The whole feed-forward sub-block of a width-256 row in one kernel:
+//   x += GELU(inv * x16 W1^T + b1) W2^T + b2, then x16 and inv of the new x.
+// The hidden activations stay on chip.  x16: 16-bit rows, box 64x128, 128B
+// swizzle; w1: W1 [F][256], box 64x128; w2: W2 [256][F], box 64x256; res: fp32
+// x, box 32x32, 128B swizzle; out16: x16 again, box 32x32, 64B swizzle.
+struct FfnMaps {
+  CUtensorMap x16, w1, w2, res, out16;
+};
+// args: m_rows, num_tiles (= ceil(m_rows / 128)), row_inv (read), row_inv_out
+// (written), bias1 = b1, bias = b2, out = the fp32 x (for an L2 prefetch), err.
+// hidden = F (a multiple of 128).
+cudaError_t launch_ffn(bool bf16, const FfnMaps& maps, const GemmArgs& args, int hidden, int sm_count,
+                       cudaStream_t stream);
 
 // ------------------------------------------------------------------ attention
 struct AttnArgs {
@@ -209,6 +225,7 @@ struct AxialWeights {
   const CUtensorMap* m_out;
   const CUtensorMap* m_ff1;
   const CUtensorMap* m_ff2;
+  const void* ff1_w;  // W1 itself (the fused FFN maps it in 128-row boxes)
   const float* gate_b;
   const float* ff1_b;
   const float* ff2_b;

@@ -332,6 +332,9 @@ def forward_flops(cfg: StackConfig, clips: int, frames: int) -> dict:
         "ff1 gemm": 2 * tokens * d * cfg.ff1_rows,
         "ff2 gemm": 2 * tokens * cfg.ff_inner * d,
     }
+    if d == 256 and cfg.ff1_rows == cfg.ff_inner and cfg.ff_inner % 128 == 0:
+        # One fused launch (FF1, GELU and FF2 with the hidden on chip).
+        per_block["ffn"] = per_block.pop("ff1 gemm") + per_block.pop("ff2 gemm")
     out = {k: v * 2 * cfg.depth for k, v in per_block.items()}
     out["attention (L>128)"] = cfg.depth * 4 * inner * clips * cfg.bands * frames * frames
     out["attention (L<=128)"] = cfg.depth * 4 * inner * clips * frames * cfg.bands * cfg.bands

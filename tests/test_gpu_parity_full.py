@@ -146,3 +146,43 @@ def test_chunked_demix_at_full_chunk_size(providers):
     print(f"30 s chunked vs demix of the provider's chunks: SNR {snr:.1f} dB")
     assert snr > 90
     assert np.abs(ref - vocals).max() <= MAX_ABS_BAR
+
+
+SPLIT_FFN_SCRIPT = r"""
+import sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from karaoke_platform_sidecar_native_b200 import modelpack, native
+from tests.golden.make_golden import LARGE_CASES, large_input
+spec, recipe, _ = LARGE_CASES[sys.argv[2]]
+p = native.Provider(0)
+p.load_model(modelpack.synthetic_pack(**getattr(modelpack, recipe + "_RECIPE")))
+np.save(sys.argv[3], p.separate(large_input(spec)))
+p.close()
+"""
+
+
+@pytest.mark.parametrize("case", ["cfg2_chunk13_test"])
+def test_fused_and_split_ffn_agree(providers, case, tmp_path):
+    # The width-256 FFN runs as one fused kernel (hidden on chip); with
+    # VOCALARC_B200_FFN=split it runs as the FF1 and FF2 GEMMs with the hidden
+    # in HBM.  Both meet the bar against the reference and agree with each
+    # other to well inside it (same K order, same 16-bit hidden rounding).
+    import subprocess
+    import sys
+    from tests.conftest import ROOT
+    g, audio, recipe = golden(case)
+    fused = providers[recipe].separate(audio)
+    out = tmp_path / "split.npy"
+    env = dict(os.environ, VOCALARC_B200_FFN="split")
+    subprocess.run([sys.executable, "-c", SPLIT_FFN_SCRIPT, ROOT, case, str(out)], env=env, check=True,
+                   timeout=600)
+    split = np.load(out)
+    for name, v in (("fused", fused), ("split", split)):
+        snr = snr_db(g["vocals"], v)
+        err = float(np.abs(g["vocals"] - v).max())
+        print(f"{case} {name} FFN: SNR {snr:.1f} dB, max abs {err:.2e}")
+        assert snr >= SNR_BAR_DB and err <= MAX_ABS_BAR
+    diff = float(np.abs(fused - split).max())
+    print(f"{case}: fused vs split FFN max abs {diff:.2e}, bit-identical {np.array_equal(fused, split)}")
+    assert snr_db(split, fused) > 80
