@@ -9,6 +9,7 @@
 // chip, otherwise the FFN input GEMM (bias + GELU, or GEGLU) and the FFN output
 // GEMM with the residual and row statistics.  RMSNorm gammas are folded into
 // the weights.
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 
@@ -54,6 +55,22 @@ bool ffn_fused_enabled() {
 
 }  // namespace
 
+// cos/sin exactly as apply_rotary builds them (vocalarc_separation.c:726-731,
+// frequencies from fill_frequencies :1312-1314), float arithmetic and libm;
+// slot q of position p holds pairs 2q and 2q + 1.
+std::vector<float4> rope_table(int n) {
+  std::vector<float4> table(static_cast<size_t>(n) * 16);
+  float freq[32];
+  for (int i = 0; i < 32; ++i) freq[i] = 1.0f / powf(10000.0f, static_cast<float>(2 * i) / kDimHead);
+  for (int p = 0; p < n; ++p)
+    for (int q = 0; q < 16; ++q) {
+      const float a0 = static_cast<float>(p) * freq[2 * q];
+      const float a1 = static_cast<float>(p) * freq[2 * q + 1];
+      table[static_cast<size_t>(q) * n + p] = make_float4(cosf(a0), sinf(a0), cosf(a1), sinf(a1));
+    }
+  return table;
+}
+
 bool run_axial_block(const AxialBuffers& b, const AxialWeights& w, const AxialShape& sh, long long tokens,
                      const AxisPlan& ax, bool bf16, int sm_count, cudaStream_t stream, LaunchHook hook,
                      void* owner) {
@@ -68,6 +85,7 @@ bool run_axial_block(const AxialBuffers& b, const AxialWeights& w, const AxialSh
   args.num_tiles = static_cast<int>((tokens + 127) / 128) * (args.n_tiles + 1);
   args.row_inv = b.row_inv;
   args.rope = b.rope;
+  args.rope_stride = b.rope_stride;
   args.pos_div = ax.pos_div;
   args.pos_mod = ax.pos_mod;
   args.rope_cols = 2 * kDimInner;

@@ -659,9 +659,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (EPI == kEpiQkvRope) {
         const bool do_rope = valid && ti.n_size == kBN && ti.n0 < args.rope_cols;
         const int pos = static_cast<int>((R / args.pos_div) % args.pos_mod);
-        const float4* table = reinterpret_cast<const float4*>(args.rope + static_cast<long long>(pos) * (kDimHead / 2));
+        const float4* table = args.rope + pos;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) rope[i] = do_rope ? __ldg(table + i) : make_float4(1.f, 0.f, 1.f, 0.f);
+        for (int i = 0; i < 16; ++i)
+          rope[i] = do_rope ? __ldg(table + static_cast<long long>(i) * args.rope_stride) : make_float4(1.f, 0.f, 1.f, 0.f);
       }
       if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, args.err, kErrWaitEpilogue)) break;
       tc_fence_after();

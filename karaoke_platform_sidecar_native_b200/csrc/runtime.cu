@@ -179,7 +179,7 @@ struct native_gpu {
   int* d_err = nullptr;
   float* d_window = nullptr;
   float2* d_twiddle = nullptr;
-  float2* d_rope = nullptr;
+  float4* d_rope = nullptr;
   int rope_len = 0;
   // workspace (grow-only)
   long long ws_tokens = 0;
@@ -366,22 +366,15 @@ bool ensure_audio(native_gpu* g, long long samples) {
   return true;
 }
 
-// cos/sin table exactly as apply_rotary builds it (vocalarc_separation.c:726-731,
-// frequencies from fill_frequencies :1312-1314), float arithmetic and libm.
+// The RoPE cos/sin table (rope_table, apply_rotary's arithmetic) for at least
+// `positions` positions.
 bool ensure_rope(native_gpu* g, int positions) {
   if (positions <= g->rope_len) return true;
   const int n = positions < 128 ? 128 : positions;
-  std::vector<float2> table(static_cast<size_t>(n) * 32);
-  float freq[32];
-  for (int i = 0; i < 32; ++i) freq[i] = 1.0f / powf(10000.0f, static_cast<float>(2 * i) / kDimHead);
-  for (int p = 0; p < n; ++p)
-    for (int i = 0; i < 32; ++i) {
-      const float angle = static_cast<float>(p) * freq[i];
-      table[static_cast<size_t>(p) * 32 + i] = make_float2(cosf(angle), sinf(angle));
-    }
+  const std::vector<float4> table = rope_table(n);
   g->rope_len = 0;
-  if (!grow(g, &g->d_rope, table.size() * sizeof(float2), "cudaMalloc(rope)")) return false;
-  if (!cuda_ok(g, cudaMemcpy(g->d_rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope"))
+  if (!grow(g, &g->d_rope, table.size() * sizeof(float4), "cudaMalloc(rope)")) return false;
+  if (!cuda_ok(g, cudaMemcpy(g->d_rope, table.data(), table.size() * sizeof(float4), cudaMemcpyHostToDevice), "rope"))
     return false;
   g->rope_len = n;
   return true;
@@ -602,7 +595,8 @@ bool provider_hook(void* owner, cudaError_t e, const char* what) {
 // updated x.
 bool run_block(native_gpu* g, const BlockW& w, long long tokens, const AxisPlan& ax) {
   if (!ensure_rope(g, ax.length) || !ensure_stats(g, tokens)) return false;
-  const AxialBuffers buf{g->x, g->x16, g->row_inv, nullptr, g->qkv, g->attn, g->gates, g->d_rope, g->d_err};
+  const AxialBuffers buf{g->x,     g->x16,    g->row_inv, nullptr,     g->qkv,
+                         g->attn,  g->gates,  g->d_rope,  g->d_err,    g->rope_len};
   const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.ff1, w.gate_b, w.ff1_b, w.ff2_b};
   if (!run_axial_block(buf, aw, AxialShape{kDim, kFfDim, 0}, tokens, ax, g->bf16 != 0, g->sm_count, g->stream,
                        provider_hook, g))

@@ -110,7 +110,7 @@ struct vocalarc_b200_stack {
   int* d_err = nullptr;
   float* d_window = nullptr;
   float2* d_twiddle = nullptr;
-  float2* d_rope = nullptr;
+  float4* d_rope = nullptr;
   int rope_len = 0;
   // weights
   void* model_mem = nullptr;
@@ -417,22 +417,15 @@ bool init_stack(Stack* s, int device) {
          sok(s, cudaMemcpy(s->d_twiddle, tw.data(), 1025 * sizeof(float2), cudaMemcpyHostToDevice), "twiddle");
 }
 
-// RoPE cos/sin table, the bundled provider's float arithmetic (apply_rotary,
+// RoPE cos/sin table, the bundled provider's (rope_table: apply_rotary,
 // vocalarc_separation.c:726-731; fill_frequencies :1312-1314).
 bool ensure_rope_s(Stack* s, int positions) {
   if (positions <= s->rope_len) return true;
   const int n = positions < 128 ? 128 : positions;
-  std::vector<float2> table(static_cast<size_t>(n) * 32);
-  float freq[32];
-  for (int i = 0; i < 32; ++i) freq[i] = 1.0f / powf(10000.0f, static_cast<float>(2 * i) / kDimHead);
-  for (int q = 0; q < n; ++q)
-    for (int i = 0; i < 32; ++i) {
-      const float angle = static_cast<float>(q) * freq[i];
-      table[static_cast<size_t>(q) * 32 + i] = make_float2(cosf(angle), sinf(angle));
-    }
+  const std::vector<float4> table = rope_table(n);
   s->rope_len = 0;
-  if (!sgrow(s, &s->d_rope, table.size() * sizeof(float2), "cudaMalloc(rope)")) return false;
-  if (!sok(s, cudaMemcpy(s->d_rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope"))
+  if (!sgrow(s, &s->d_rope, table.size() * sizeof(float4), "cudaMalloc(rope)")) return false;
+  if (!sok(s, cudaMemcpy(s->d_rope, table.data(), table.size() * sizeof(float4), cudaMemcpyHostToDevice), "rope"))
     return false;
   s->rope_len = n;
   return true;
@@ -505,7 +498,8 @@ bool stack_hook(void* owner, cudaError_t e, const char* what) {
 bool run_block_s(Stack* s, const StackBlock& w, long long tokens, const AxisPlan& ax) {
   const StackShape& sh = s->shape;
   if (!ensure_rope_s(s, ax.length)) return false;
-  const AxialBuffers buf{s->x, s->x16, s->row_inv, s->sumsq, s->wide, s->attn, s->gates, s->d_rope, s->d_err};
+  const AxialBuffers buf{s->x,    s->x16,   s->row_inv, s->sumsq, s->wide,
+                         s->attn, s->gates, s->d_rope,  s->d_err, s->rope_len};
   const AxialWeights aw{&w.m_qkv, &w.m_out, &w.m_ff1, &w.m_ff2, w.ff1, w.gate_b, w.ff1_b, w.ff2_b};
   return run_axial_block(buf, aw, AxialShape{sh.dim, sh.ff_inner, sh.geglu}, tokens, ax, s->bf16 != 0, s->sm_count,
                          s->stream, stack_hook, s);

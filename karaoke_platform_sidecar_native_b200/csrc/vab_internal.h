@@ -2,6 +2,7 @@
 #pragma once
 
 #include <atomic>
+#include <vector>
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
@@ -76,7 +77,11 @@ struct GemmArgs {
   const float* bias;
   const float* row_inv;  // per-row RMSNorm factor applied to the accumulator (null = 1)
   float* row_inv_out;    // kEpiResidual: per-row factor of the updated residual
-  const float2* rope;   // [positions][32] (cos, sin)
+  // RoPE (cos, sin) in slot-major order: rope[q * rope_stride + pos] holds
+  // pairs 2q and 2q + 1 of position pos, so the 32 rows of a warp (consecutive
+  // positions on the time axis) read 512 contiguous bytes per slot.
+  const float4* rope;
+  int rope_stride;
   int pos_div;
   int pos_mod;
   int rope_cols;
@@ -241,9 +246,14 @@ struct AxialBuffers {
   void* wide;
   void* attn;
   float* gates;
-  const float2* rope;
+  const float4* rope;   // slot-major RoPE table (rope_table), rope_stride positions
   int* err;
+  int rope_stride;
 };
+// The RoPE (cos, sin) table for positions [0, n) in the slot-major layout the
+// QKV epilogue reads (GemmArgs::rope): n * 16 float4.
+std::vector<float4> rope_table(int n);
+
 struct AxialShape {
   int dim;        // 256 or 512
   int ff_inner;   // FFN hidden width
