@@ -144,7 +144,10 @@ int vocalarc_b200_range_owned(const native_gpu *gpu, int *s0, int *s1);
    process.  The seam stays valid until this provider's next range_forward. */
 int vocalarc_b200_range_seam_export(native_gpu *gpu, void *handle);
 /* Copies the previous range's seam from its exported handle (another process,
-   any GPU of the node) into this GPU's memory. */
+   any GPU of the node) into this GPU's memory.  The handle's mapping is kept
+   for later imports of the same handle (the exporter keeps its seam buffer
+   while its range geometry does not grow) and released when a different
+   handle arrives or this provider is destroyed. */
 int vocalarc_b200_range_seam_import(native_gpu *gpu, const void *handle);
 /* Same, from a provider of this process (same or another GPU). */
 int vocalarc_b200_range_seam_from(native_gpu *gpu, const native_gpu *prev);

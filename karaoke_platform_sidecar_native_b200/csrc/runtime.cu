@@ -237,6 +237,10 @@ struct native_gpu {
   float* seam_in = nullptr;     // the previous range's seam, copied here
   long long seam_cap = 0;       // floats allocated in each seam buffer
   int has_seam_in = 0;
+  // The previous range's seam buffer in another process, mapped once per
+  // exported handle (opening an IPC mapping costs far more than the copy).
+  void* seam_peer = nullptr;
+  unsigned char seam_peer_handle[64] = {};
   // bigshift + TTA variant tracks and their estimates (vocalarc_b200_separate_tta)
   long long ws_tta = 0;
   float* tta_in = nullptr;
@@ -1309,6 +1313,7 @@ void native_gpu_destroy(native_gpu* g) {
   if (g == nullptr) return;
   cudaSetDevice(g->device);
   if (g->stream != nullptr) cudaStreamSynchronize(g->stream);
+  if (g->seam_peer != nullptr) cudaIpcCloseMemHandle(g->seam_peer);
   void* ptrs[] = {g->x, g->x_alt, g->x16, g->row_inv, g->qkv, g->attn, g->gates, g->spec, g->mask, g->frames_buf,
                   g->seg_out, g->audio_in, g->audio_out, g->d_tiles1, g->d_tiles2, g->d_err, g->d_window,
                   g->d_twiddle, g->d_rope, g->abi_mask_mem, g->seam_out, g->seam_in, g->tta_in, g->tta_out,
@@ -1845,17 +1850,25 @@ int vocalarc_b200_range_seam_export(native_gpu* g, void* handle) {
 int vocalarc_b200_range_seam_import(native_gpu* g, const void* handle) {
   if (!active(g) || !g->range_ready || handle == nullptr || g->range_c0 == 0) return 0;
   cudaSetDevice(g->device);
-  cudaIpcMemHandle_t h;
-  memcpy(&h, handle, sizeof(h));
-  void* peer = nullptr;
-  if (!cuda_ok(g, cudaIpcOpenMemHandle(&peer, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle(seam)"))
-    return 0;
+  static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(g->seam_peer_handle), "IPC handle size");
+  if (g->seam_peer == nullptr || memcmp(g->seam_peer_handle, handle, sizeof(g->seam_peer_handle)) != 0) {
+    // A new exported buffer: drop the old mapping, map this one.
+    if (g->seam_peer != nullptr) cudaIpcCloseMemHandle(g->seam_peer);
+    g->seam_peer = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* peer = nullptr;
+    if (!cuda_ok(g, cudaIpcOpenMemHandle(&peer, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle(seam)"))
+      return 0;
+    g->seam_peer = peer;
+    memcpy(g->seam_peer_handle, handle, sizeof(g->seam_peer_handle));
+  }
   const size_t bytes = static_cast<size_t>(g->range_chunk - g->range_step) * 3 * 4;
   // Peer copy over NVLink into this GPU's memory; the previous range's
   // provider keeps the buffer until every range has finished.
-  const bool ok = cuda_ok(g, cudaMemcpyAsync(g->seam_in, peer, bytes, cudaMemcpyDefault, g->stream), "seam copy") &&
-                  sync_and_check(g, "seam copy");
-  cudaIpcCloseMemHandle(peer);
+  const bool ok =
+      cuda_ok(g, cudaMemcpyAsync(g->seam_in, g->seam_peer, bytes, cudaMemcpyDefault, g->stream), "seam copy") &&
+      sync_and_check(g, "seam copy");
   if (!ok) return 0;
   g->has_seam_in = 1;
   return 1;
