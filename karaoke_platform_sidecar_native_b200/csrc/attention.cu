@@ -71,6 +71,10 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // rest to MUFU ex2 (16 results per clock per SM), balancing the two pipes;
 // 2 of 8 measured fastest against 0, 3 and 4.
 constexpr int kPolyPairs = 2;
+// The band-axis kernel is paced by its per-item latency, not by MUFU: all its
+// exponentials go to MUFU (0 of 8 measured 0.564 ms against 0.588, 0.71 and
+// 0.72 ms for 2, 1 and 3 of 8 on 4 chunks at L = 90).
+constexpr int kItemPolyPairs = 0;
 
 // ---------------------------------------------------------------------------
 // Long sequences (L > 128): a persistent CTA walks units of two 128-query
@@ -915,7 +919,7 @@ __global__ void __launch_bounds__(kItemThreads, 1)
             if (q < width) {
               const float2 x2 = __ffma2_rn(make_float2(v[q], v[q + 1]), c2, nm2);
               float2 p2;
-              if (((q >> 1) & 7) < kPolyPairs) {
+              if (((q >> 1) & 7) < kItemPolyPairs) {
                 p2 = exp2_poly2(x2);
               } else {
                 p2.x = ex2_approx(x2.x);
