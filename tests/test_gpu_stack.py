@@ -166,3 +166,32 @@ def test_config3_full_size_is_deterministic():
     assert torch.isfinite(outs[0]).all()
     assert torch.equal(outs[0], outs[1])
     assert float(outs[0].abs().max()) > 0
+
+
+SMALL_BUNDLED = st.BUNDLED.replace(depth=1)
+
+
+@pytest.mark.parametrize("bf16", [True, False], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_block_fused_ffn_dim256(bf16, axis):
+    # Width 256 with a GELU FFN runs the fused FFN kernel (FF1, GELU and FF2
+    # with the hidden on chip); both operand types against the stack oracle.
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    cfg = SMALL_BUNDLED.replace(bf16=bf16)
+    weights = st.synthetic_weights(cfg, seed=4, gamma_sigma=0.1, bias_sigma=0.02)
+    w = st.split_weights(cfg, weights)
+    length = 512 * 150 + 77
+    audio = fixtures.tone_mix(seconds=length / 44100 + 0.01, seed=21)[:, :length]
+    clips2 = np.ascontiguousarray(np.stack([audio, audio[::-1]]), dtype=np.float32)
+    frames = cfg.frames(length)
+    xs = [SO.band_split(cfg, w, O.stft(clips2[c], cfg.hop)) for c in range(2)]
+    s = st.Stack(cfg, weights)
+    try:
+        x = torch.from_numpy(np.stack(xs)).cuda()
+        run(s, s.stage_block, x, 2, frames, 0, axis)
+        bar = 45 if bf16 else 60
+        for c in range(2):
+            assert snr_db(SO.block(cfg, w, 0, axis, xs[c]), x[c].cpu().numpy()) > bar
+    finally:
+        s.close()
