@@ -1,4 +1,6 @@
-// Persistent tcgen05 GEMM for sm_100a:  C[M][N] = A[M][K] * B[N][K]^T.
+// Persistent tcgen05 GEMM for sm_100a:  C[M][N] = A[M][K] * B[N][K]^T, and
+// (ffn_kernel, further down) the fused feed-forward sub-block of a width-256
+// row, FF1 -> GELU -> FF2 + residual with the hidden kept on chip.
 //
 // One CTA per SM walks a static tile schedule.  Warp 0 issues TMA loads of
 // 128x64 A and (n_size)x64 B tiles into a 3-stage 128-byte-swizzled ring, warp
