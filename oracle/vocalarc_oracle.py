@@ -318,13 +318,21 @@ def chunk_plan(length: int, chunk: int = CHUNK_SAMPLES, step: int | None = None)
     return border, padded, starts
 
 
-def chunk_weights(count: int, chunk: int, batch: int = 1) -> np.ndarray:
+def chunk_weights(count: int, chunk: int, batch: int = 1, fade_ramp: np.ndarray | None = None) -> np.ndarray:
     """Per-chunk OLA weights ``[count][chunk]``: linear fade over the last chunk/10
     samples, forced to 1 for chunks of the first and the final predict batch
-    (onnx_sidecar.cpp:740-767; ``batch`` is the sidecar's model batch size)."""
+    (onnx_sidecar.cpp:740-767; ``batch`` is the sidecar's model batch size).
+
+    ``fade_ramp`` (chunk/10 values) replaces the sidecar's ramp 1 - i/fade
+    (:741-742).  The reference's Python twin of this loop (onnx/audio.py:153-154)
+    uses linspace(1, 0, fade) instead; the tests pass that ramp to compare the
+    rest of the assembly with the twin's own output."""
     fade = chunk // 10
     base = np.ones(chunk, dtype=F32)
-    base[chunk - fade:] = (F32(1.0) - np.arange(fade, dtype=F32) / F32(fade)).astype(F32)
+    if fade_ramp is None:
+        base[chunk - fade:] = (F32(1.0) - np.arange(fade, dtype=F32) / F32(fade)).astype(F32)
+    elif fade > 0:
+        base[chunk - fade:] = np.asarray(fade_ramp, dtype=F32)
     weights = np.repeat(base[None, :], count, axis=0)
     step_batches = [list(range(i, min(i + batch, count))) for i in range(0, count, batch)]
     for b_index, members in enumerate(step_batches):
@@ -335,8 +343,10 @@ def chunk_weights(count: int, chunk: int, batch: int = 1) -> np.ndarray:
     return weights
 
 
-def demix(predict, mix: np.ndarray, chunk: int = CHUNK_SAMPLES, batch: int = 1) -> np.ndarray:
-    """Chunked overlap-add (``Separator::demix`` onnx_sidecar.cpp:725-782)."""
+def demix(predict, mix: np.ndarray, chunk: int = CHUNK_SAMPLES, batch: int = 1,
+          fade_ramp: np.ndarray | None = None) -> np.ndarray:
+    """Chunked overlap-add (``Separator::demix`` onnx_sidecar.cpp:725-782);
+    ``fade_ramp`` as in ``chunk_weights``."""
     mix = np.asarray(mix, dtype=F32)
     length = mix.shape[1]
     border, padded, plan = chunk_plan(length, chunk)
@@ -345,7 +355,7 @@ def demix(predict, mix: np.ndarray, chunk: int = CHUNK_SAMPLES, batch: int = 1) 
         working = mix[:, idx]
     else:
         working = mix
-    weights = chunk_weights(len(plan), chunk, batch)
+    weights = chunk_weights(len(plan), chunk, batch, fade_ramp)
     result = np.zeros((CHANNELS, padded), dtype=F32)
     counter = np.zeros((CHANNELS, padded), dtype=F32)
     for index, (start, valid) in enumerate(plan):
