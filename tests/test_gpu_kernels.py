@@ -104,6 +104,27 @@ def test_attention_matches_fp32_softmax(provider, d1, d2, d3, pos_dim):
     assert float((out.float() - ref).abs().mean() / ref.abs().mean()) < 2e-3
 
 
+@pytest.mark.parametrize("d1,d2", [(1722, 2), (300, 3)])
+def test_attention_rising_scores(provider, d1, d2):
+    # Keys grow along the sequence (x1 to x7), so later key tiles score far
+    # above a row's first tile: the time-axis kernel must raise its reference
+    # maximum again and again, rescaling O in tensor memory and the packed P of
+    # the tile's first half.
+    rows = d1 * d2
+    g = torch.Generator(device="cuda").manual_seed(7 + d1)
+    qkv = torch.randn(rows, 1536, device="cuda", generator=g)
+    ramp = 1.0 + 6.0 * torch.arange(d1, device="cuda", dtype=torch.float32) / d1
+    qkv[:, 512:1024] *= ramp.repeat(d2)[:, None]
+    qkv = qkv.half()
+    gates = torch.rand(rows, 8, device="cuda", generator=g)
+    out = torch.full((rows, 512), float("nan"), device="cuda", dtype=torch.float16)
+    run(provider, provider.stage_attention, qkv, gates, out, d1, d2, 1, 1)
+    ref = attention_reference(qkv, gates, d1, d2, 1, 1)
+    assert torch.isfinite(out.float()).all()
+    assert rel_max(out.float(), ref) < 1e-2
+    assert float((out.float() - ref).abs().mean() / ref.abs().mean()) < 2e-3
+
+
 def snr_db(ref, test):
     ref = np.asarray(ref, dtype=np.float64)
     err = ref - np.asarray(test, dtype=np.float64)
