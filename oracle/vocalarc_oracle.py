@@ -26,7 +26,11 @@ does), the reference CPU path of ``native/vocalarc_separation.c``:
 Parity of this restatement is pinned against the reference executable itself:
 ``tests/golden/make_golden.py`` runs the unchanged reference CPU build on the
 seeded synthetic pack and stores its stage dumps (``VOCALARC_DEBUG_DUMP``) and
-output WAV; ``tests/test_oracle.py`` compares this module against them.
+output WAV; ``tests/test_oracle.py`` compares this module against them.  The
+chunk assembly (``demix``), ``bigshift`` and ``separate_tta`` follow the C++
+ONNX sidecar, which cannot run here; ``tests/golden/make_demix_twin.py`` runs
+the reference's Python twin of that loop (onnx/audio.py) and
+``tests/test_demix_twin.py`` checks this module against it.
 
 Known intentional differences: the reference exponentials use its own
 polynomial ``fast_exp`` (:383-398) and its FFT is a radix-2 recurrence; both
